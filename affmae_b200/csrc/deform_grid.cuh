@@ -1,0 +1,136 @@
+// Uniform-grid spatial index of 2-D point sets (one grid per batch element)
+// and an exact 4-nearest-neighbour query on it.
+//
+// The fused deformable attention of the reference
+// (src/layers/kernels/fused_deform_attn.py:1085-1125, :1273-1290) finds the
+// 4 nearest kv positions of every sample point by scanning all Nkv points
+// (O(Nq*Nkv*H*4)).  Here the kv points are bucketed once per call into a
+// G x G grid over their bounding box (counting sort: count, scan, scatter),
+// and each sample visits grid rings around its cell until the distance to
+// the unvisited region exceeds its current 4th-best distance.  Candidates are
+// ranked by (fp32 squared distance, index) lexicographically, which is
+// exactly the order produced by the reference's ascending-index scan with a
+// strict '<' insertion, so the selected neighbours and their order match the
+// brute-force result bit for bit.
+#pragma once
+
+#include "common.cuh"
+
+namespace affb {
+
+struct GridView {
+  const float* params;   // [B][8]: minx, miny, cw, ch, inv_cw, inv_ch, -, -
+  const int32_t* start;  // [B][G*G+1]
+  const float4* pts;     // [B][Nkv]: x, y, index bits, 0
+  int G;
+  int64_t Nkv;
+};
+
+// Grid side: about two points per cell.
+__host__ __device__ inline int grid_side(int64_t nkv) {
+  int64_t g = 1;
+  while (g * g * 2 < nkv && g < 4096) ++g;
+  return (int)g;
+}
+
+__host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) & ~(int64_t)255; }
+
+struct GridLayout {
+  int G;
+  int64_t off_params, off_start, off_cursor, off_pts, total;
+};
+
+// Byte layout of the grid inside a caller-provided workspace.
+__host__ __device__ inline GridLayout grid_layout(int64_t B, int64_t nkv) {
+  GridLayout L;
+  L.G = grid_side(nkv);
+  const int64_t ncell = (int64_t)L.G * L.G;
+  L.off_params = 0;
+  L.off_start = align256(B * 8 * 4);
+  L.off_cursor = L.off_start + align256(B * (ncell + 1) * 4);
+  L.off_pts = L.off_cursor + align256(B * ncell * 4);
+  L.total = L.off_pts + align256(B * nkv * 16);
+  return L;
+}
+
+__device__ __forceinline__ float sqdist2(float sx, float sy, float px, float py) {
+  const float dx = __fsub_rn(sx, px), dy = __fsub_rn(sy, py);
+  return __fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy));
+}
+
+// Top-4 under the (distance, index) order; d[0] <= d[1] <= d[2] <= d[3].
+// Empty slots hold (1e38, 0) like the reference's initial state.
+struct Top4 {
+  float d[4];
+  int i[4];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { d[k] = 1e38f; i[k] = 0; }
+  }
+  __device__ __forceinline__ static bool before(float da, int ia, float db, int ib) {
+    return da < db || (da == db && ia < ib);
+  }
+  __device__ __forceinline__ void offer(float dd, int ii) {
+    if (!before(dd, ii, d[3], i[3])) return;
+    if (before(dd, ii, d[2], i[2])) {
+      d[3] = d[2]; i[3] = i[2];
+      if (before(dd, ii, d[1], i[1])) {
+        d[2] = d[1]; i[2] = i[1];
+        if (before(dd, ii, d[0], i[0])) {
+          d[1] = d[0]; i[1] = i[0];
+          d[0] = dd; i[0] = ii;
+        } else { d[1] = dd; i[1] = ii; }
+      } else { d[2] = dd; i[2] = ii; }
+    } else { d[3] = dd; i[3] = ii; }
+  }
+};
+
+__device__ __forceinline__ int cell_coord(float f, int G) {
+  return (f >= 0.f) ? (f < (float)G ? (int)f : G - 1) : 0;
+}
+
+// Exact 4-NN of (sx, sy) among the points of batch element b.
+__device__ inline void grid_knn4(const GridView& g, int64_t b, float sx, float sy, Top4& top) {
+  top.init();
+  const float* P = g.params + b * 8;
+  const float minx = P[0], miny = P[1], cw = P[2], ch = P[3], icw = P[4], ich = P[5];
+  const int G = g.G;
+  const int32_t* st = g.start + b * ((int64_t)G * G + 1);
+  const float4* pts = g.pts + b * g.Nkv;
+  int cx = cell_coord((sx - minx) * icw, G);
+  int cy = cell_coord((sy - miny) * ich, G);
+  if (!(sx == sx) || !(sy == sy)) { cx = 0; cy = 0; }
+  // slack for the rounding of cell assignment and of boundary positions
+  const float slack = 1e-4f * fmaxf(cw, ch) +
+                      2e-6f * (fabsf(sx) + fabsf(sy) + fabsf(minx) + fabsf(miny) + G * fmaxf(cw, ch));
+  for (int r = 0; r <= G; ++r) {
+    const int x0 = cx - r, x1 = cx + r, y0 = cy - r, y1 = cy + r;
+    const int ylo = max(y0, 0), yhi = min(y1, G - 1);
+    const int xlo = max(x0, 0), xhi = min(x1, G - 1);
+    for (int yy = ylo; yy <= yhi; ++yy) {
+      const bool edge_row = (yy == y0 || yy == y1);
+      const int step = edge_row ? 1 : (x1 - x0 > 0 ? x1 - x0 : 1);
+      for (int xx = edge_row ? xlo : x0; xx <= xhi; xx += step) {
+        if (xx < 0) continue;
+        const int c = yy * G + xx;
+        const int e = st[c + 1];
+        for (int t = st[c]; t < e; ++t) {
+          const float4 q = pts[t];
+          top.offer(sqdist2(sx, sy, q.x, q.y), __float_as_int(q.z));
+        }
+      }
+    }
+    // lower bound of the distance to any point outside the visited square
+    float lb = 3.4e38f;
+    bool open = false;
+    if (x0 > 0) { lb = fminf(lb, sx - (minx + x0 * cw)); open = true; }
+    if (x1 < G - 1) { lb = fminf(lb, (minx + (x1 + 1) * cw) - sx); open = true; }
+    if (y0 > 0) { lb = fminf(lb, sy - (miny + y0 * ch)); open = true; }
+    if (y1 < G - 1) { lb = fminf(lb, (miny + (y1 + 1) * ch) - sy); open = true; }
+    if (!open) break;
+    lb -= slack;
+    if (lb > 0.f && lb * lb * (1.f - 1e-5f) > top.d[3]) break;
+  }
+}
+
+}  // namespace affb

@@ -1,0 +1,445 @@
+// Fused KNN + Shepard-weighted deformable attention (2-D, 4 points per head,
+// 4 nearest neighbours per point), forward and backward.
+//
+// Forward semantics (src/layers/kernels/fused_deform_attn.py:1342-1509, the
+// cross-attention kernel that saves its KNN; self-attention :1018-1181 is the
+// same with kv_pos = pos):
+//   s      = query_pos[n] + offsets[n,h,p]                    (fp32)
+//   {j}    = 4 nearest kv positions of s, (d2, index) order
+//   dist_j = sqrt(d2_j) + 1e-6 ;  P = max(power, 1e-6)
+//   w_j    = exp(-P dist_j - max) / (sum + 1e-8)
+//   out[n,h,:] = sum_p attn_w[n,h,p] * (w0 v_j0 + w1 v_j1 + w2 v_j2 + w3 v_j3)
+// Backward (cross :1982-2381, self :1520-1975):
+//   d_attn_w = dout . sum_j w_j v_j
+//   dp_j     = v_j . (attn_w dout);  ds_j = w_j (dp_j - sum_k w_k dp_k)
+//   d_power += sum_j ds_j * (-dist_j)
+//   d_d2_j   = (-P ds_j) / (2 dist_j)          (dist_j includes the 1e-6)
+//   d_off    = d_qpos contribution = 2 sum_j (s - kv_j) d_d2_j
+//   d_kvpos[j] += -2 (s - kv_j) d_d2_j ;  d_values[j,h] += attn_w w_j dout
+//
+// Layout: one warp per query.  Lane l owns sample l (= h*4 + p) for the
+// neighbour search and all per-sample scalar math; for the value gather and
+// scatter the lanes are re-assigned to 8-channel chunks of the query's
+// H*C output row, and per-sample scalars travel through shared memory.
+// The neighbour search uses the grid index of deform_grid.cuh, built into a
+// caller-provided workspace by four small kernels (bbox, count, scan, scatter).
+#include "deform_grid.cuh"
+
+namespace affb {
+
+constexpr int DK_WARPS = 8;
+constexpr int DK_SMAX = 64;  // samples per query (H * 4) handled per warp
+
+// ---------------------------------------------------------------- grid build
+__global__ void grid_bbox_kernel(const float* __restrict__ pos, int64_t nkv, int G,
+                                 float* __restrict__ params) {
+  const int64_t b = blockIdx.x;
+  const float* p = pos + b * nkv * 2;
+  float mnx = 3.4e38f, mny = 3.4e38f, mxx = -3.4e38f, mxy = -3.4e38f;
+  for (int64_t i = threadIdx.x; i < nkv; i += blockDim.x) {
+    const float x = p[2 * i], y = p[2 * i + 1];
+    if (x == x) { mnx = fminf(mnx, x); mxx = fmaxf(mxx, x); }
+    if (y == y) { mny = fminf(mny, y); mxy = fmaxf(mxy, y); }
+  }
+  __shared__ float red[4][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mnx = fminf(mnx, __shfl_xor_sync(0xffffffffu, mnx, o));
+    mny = fminf(mny, __shfl_xor_sync(0xffffffffu, mny, o));
+    mxx = fmaxf(mxx, __shfl_xor_sync(0xffffffffu, mxx, o));
+    mxy = fmaxf(mxy, __shfl_xor_sync(0xffffffffu, mxy, o));
+  }
+  if (lane == 0) { red[0][w] = mnx; red[1][w] = mny; red[2][w] = mxx; red[3][w] = mxy; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = blockDim.x / 32;
+    for (int i = 1; i < nw; ++i) {
+      mnx = fminf(mnx, red[0][i]); mny = fminf(mny, red[1][i]);
+      mxx = fmaxf(mxx, red[2][i]); mxy = fmaxf(mxy, red[3][i]);
+    }
+    if (!(mnx <= mxx)) { mnx = 0.f; mxx = 1.f; }
+    if (!(mny <= mxy)) { mny = 0.f; mxy = 1.f; }
+    float cw = (mxx - mnx) / G, ch = (mxy - mny) / G;
+    if (!(cw > 0.f)) cw = 1.f;
+    if (!(ch > 0.f)) ch = 1.f;
+    float* P = params + b * 8;
+    P[0] = mnx; P[1] = mny; P[2] = cw; P[3] = ch; P[4] = 1.f / cw; P[5] = 1.f / ch;
+    P[6] = 0.f; P[7] = 0.f;
+  }
+}
+
+__device__ __forceinline__ int cell_of(const float* P, int G, float x, float y) {
+  int cx = cell_coord((x - P[0]) * P[4], G);
+  int cy = cell_coord((y - P[1]) * P[5], G);
+  if (!(x == x) || !(y == y)) { cx = 0; cy = 0; }
+  return cy * G + cx;
+}
+
+__global__ void grid_count_kernel(const float* __restrict__ pos, int64_t B, int64_t nkv, int G,
+                                  const float* __restrict__ params, int32_t* __restrict__ cnt) {
+  const int64_t ncell = (int64_t)G * G;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < B * nkv;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = t / nkv;
+    const int c = cell_of(params + b * 8, G, pos[2 * t], pos[2 * t + 1]);
+    atomicAdd(cnt + b * ncell + c, 1);
+  }
+}
+
+// Exclusive scan of the per-cell counts of one batch element (one block of
+// 1024 threads).  Writes start[] and turns the counts into scatter cursors.
+__global__ void grid_scan_kernel(int G, int32_t* __restrict__ cnt_cursor, int32_t* __restrict__ start) {
+  const int64_t b = blockIdx.x;
+  const int64_t ncell = (int64_t)G * G;
+  int32_t* c = cnt_cursor + b * ncell;
+  int32_t* s = start + b * (ncell + 1);
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int64_t base = 0; base < ncell; base += blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    const int32_t v = i < ncell ? c[i] : 0;
+    int32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int32_t t = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      if (lane < nw) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const int32_t excl = carry + (w > 0 ? warp_tot[w - 1] : 0) + x - v;
+    if (i < ncell) { s[i] = excl; c[i] = excl; }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) s[ncell] = carry;
+}
+
+__global__ void grid_scatter_kernel(const float* __restrict__ pos, int64_t B, int64_t nkv, int G,
+                                    const float* __restrict__ params, int32_t* __restrict__ cursor,
+                                    float4* __restrict__ pts) {
+  const int64_t ncell = (int64_t)G * G;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < B * nkv;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = t / nkv;
+    const float x = pos[2 * t], y = pos[2 * t + 1];
+    const int c = cell_of(params + b * 8, G, x, y);
+    const int slot = atomicAdd(cursor + b * ncell + c, 1);
+    pts[b * nkv + slot] = make_float4(x, y, __int_as_float((int)(t - b * nkv)), 0.f);
+  }
+}
+
+static int build_grid(const float* kv_pos, int64_t B, int64_t nkv, void* ws, GridView& gv,
+                      cudaStream_t st) {
+  const GridLayout L = grid_layout(B, nkv);
+  char* base = (char*)ws;
+  float* params = (float*)(base + L.off_params);
+  int32_t* start = (int32_t*)(base + L.off_start);
+  int32_t* cursor = (int32_t*)(base + L.off_cursor);
+  float4* pts = (float4*)(base + L.off_pts);
+  const int64_t ncell = (int64_t)L.G * L.G;
+  if (cudaMemsetAsync(cursor, 0, B * ncell * 4, st) != cudaSuccess) {
+    set_error("deform grid: memset failed");
+    return AFFB_ERR_CUDA;
+  }
+  grid_bbox_kernel<<<(unsigned)B, 512, 0, st>>>(kv_pos, nkv, L.G, params);
+  const int64_t tot = B * nkv;
+  unsigned nb = (unsigned)imin64((tot + 255) / 256, (int64_t)sm_count() * 16);
+  if (nb == 0) nb = 1;
+  grid_count_kernel<<<nb, 256, 0, st>>>(kv_pos, B, nkv, L.G, params, cursor);
+  grid_scan_kernel<<<(unsigned)B, 1024, 0, st>>>(L.G, cursor, start);
+  grid_scatter_kernel<<<nb, 256, 0, st>>>(kv_pos, B, nkv, L.G, params, cursor, pts);
+  gv.params = params;
+  gv.start = start;
+  gv.pts = pts;
+  gv.G = L.G;
+  gv.Nkv = nkv;
+  return AFFB_OK;
+}
+
+// ------------------------------------------------------------ attention
+__device__ __forceinline__ void shepard4(const float* d2, float P, float* w, float* dist) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) dist[j] = sqrtf(d2[j]) + 1e-6f;
+  float lg[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) lg[j] = -P * dist[j];
+  const float mx = fmaxf(fmaxf(lg[0], lg[1]), fmaxf(lg[2], lg[3]));
+  float e[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) e[j] = expf(lg[j] - mx);
+  const float sum = e[0] + e[1] + e[2] + e[3] + 1e-8f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = e[j] / sum;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(DK_WARPS * 32)
+deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ offsets,
+                      const float* __restrict__ attn_w, const T* __restrict__ values,
+                      const float* __restrict__ power, int64_t B, int64_t Nq, int64_t Nkv, int H,
+                      int C, GridView gv, T* __restrict__ out, int32_t* __restrict__ knn_idx,
+                      float* __restrict__ knn_d2) {
+  __shared__ int s_idx[DK_WARPS][DK_SMAX * 4];
+  __shared__ float s_w[DK_WARPS][DK_SMAX * 4];
+  __shared__ float s_aw[DK_WARPS][DK_SMAX];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t gq = (int64_t)blockIdx.x * DK_WARPS + warp;
+  if (gq >= B * Nq) return;
+  const int64_t b = gq / Nq;
+  const float P = fmaxf(power[0], 1e-6f);
+  const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
+  const int S = H * 4;
+  for (int s = lane; s < S; s += 32) {
+    const int64_t gs = gq * S + s;
+    const float sx = __fadd_rn(qx, offsets[2 * gs]);
+    const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
+    Top4 top;
+    grid_knn4(gv, b, sx, sy, top);
+    reinterpret_cast<int4*>(knn_idx)[gs] = make_int4(top.i[0], top.i[1], top.i[2], top.i[3]);
+    reinterpret_cast<float4*>(knn_d2)[gs] = make_float4(top.d[0], top.d[1], top.d[2], top.d[3]);
+    float w[4], dist[4];
+    shepard4(top.d, P, w, dist);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s_idx[warp][s * 4 + j] = top.i[j];
+      s_w[warp][s * 4 + j] = w[j];
+    }
+    s_aw[warp][s] = attn_w[gs];
+  }
+  __syncwarp();
+  const int row = H * C;
+  const T* vb = values + b * Nkv * row;
+  for (int c8 = lane; c8 * 8 < row; c8 += 32) {
+    const int h = (c8 * 8) / C;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int si = h * 4 + p;
+      float wv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wv[e] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int id = s_idx[warp][si * 4 + j];
+        const float w = s_w[warp][si * 4 + j];
+        float v[8];
+        ld8(vb + (int64_t)id * row + c8 * 8, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = fmaf(w, v[e], wv[e]);
+      }
+      const float aw = s_aw[warp][si];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(aw, wv[e], acc[e]);
+    }
+    st8(out + gq * row + c8 * 8, acc);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(DK_WARPS * 32)
+deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ kvpos,
+                      const float* __restrict__ offsets, const float* __restrict__ attn_w,
+                      const T* __restrict__ values, const float* __restrict__ power,
+                      const int32_t* __restrict__ knn_idx, const float* __restrict__ knn_d2,
+                      const T* __restrict__ dout, int64_t B, int64_t Nq, int64_t Nkv, int H, int C,
+                      float* __restrict__ d_off, float* __restrict__ d_aw,
+                      float* __restrict__ d_qpos, float* __restrict__ d_kvpos,
+                      float* __restrict__ d_val, float* __restrict__ d_power) {
+  __shared__ int s_idx[DK_WARPS][DK_SMAX * 4];
+  __shared__ float s_w[DK_WARPS][DK_SMAX * 4];
+  __shared__ float s_dot[DK_WARPS][DK_SMAX * 4];
+  __shared__ float s_aw[DK_WARPS][DK_SMAX];
+  __shared__ float s_datt[DK_WARPS][DK_SMAX];
+  __shared__ float s_pow[DK_WARPS];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float P = fmaxf(power[0], 1e-6f);
+  const int S = H * 4;
+  const int row = H * C;
+  float dpow = 0.f;
+  for (int64_t gq = (int64_t)blockIdx.x * DK_WARPS + warp; gq < B * Nq;
+       gq += (int64_t)gridDim.x * DK_WARPS) {
+    const int64_t b = gq / Nq;
+    for (int s = lane; s < S; s += 32) {
+      const int64_t gs = gq * S + s;
+      const int4 ii = reinterpret_cast<const int4*>(knn_idx)[gs];
+      const float4 dd = reinterpret_cast<const float4*>(knn_d2)[gs];
+      const float d2[4] = {dd.x, dd.y, dd.z, dd.w};
+      float w[4], dist[4];
+      shepard4(d2, P, w, dist);
+      s_idx[warp][s * 4 + 0] = ii.x; s_idx[warp][s * 4 + 1] = ii.y;
+      s_idx[warp][s * 4 + 2] = ii.z; s_idx[warp][s * 4 + 3] = ii.w;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { s_w[warp][s * 4 + j] = w[j]; s_dot[warp][s * 4 + j] = 0.f; }
+      s_aw[warp][s] = attn_w[gs];
+      s_datt[warp][s] = 0.f;
+    }
+    __syncwarp();
+    const T* vb = values + b * Nkv * row;
+    float* dvb = d_val + b * Nkv * row;
+    for (int c8 = lane; c8 * 8 < row; c8 += 32) {
+      const int h = (c8 * 8) / C;
+      float g[8];
+      ld8(dout + gq * row + c8 * 8, g);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int si = h * 4 + p;
+        const float aw = s_aw[warp][si];
+        float datt = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int id = s_idx[warp][si * 4 + j];
+          const float w = s_w[warp][si * 4 + j];
+          float v[8];
+          ld8(vb + (int64_t)id * row + c8 * 8, v);
+          float dot = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dot = fmaf(v[e], g[e], dot);
+          atomicAdd(&s_dot[warp][si * 4 + j], dot);
+          datt = fmaf(w, dot, datt);
+          const float cf = aw * w;
+          float* dst = dvb + (int64_t)id * row + c8 * 8;
+          red_add_v4(dst, cf * g[0], cf * g[1], cf * g[2], cf * g[3]);
+          red_add_v4(dst + 4, cf * g[4], cf * g[5], cf * g[6], cf * g[7]);
+        }
+        atomicAdd(&s_datt[warp][si], datt);
+      }
+    }
+    __syncwarp();
+    float gqx = 0.f, gqy = 0.f;
+    const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
+    const float* kvb = kvpos + b * Nkv * 2;
+    float* dkvb = d_kvpos + b * Nkv * 2;
+    for (int s = lane; s < S; s += 32) {
+      const int64_t gs = gq * S + s;
+      const float sx = __fadd_rn(qx, offsets[2 * gs]);
+      const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
+      const float4 dd = reinterpret_cast<const float4*>(knn_d2)[gs];
+      const float d2[4] = {dd.x, dd.y, dd.z, dd.w};
+      float w[4], dist[4];
+      shepard4(d2, P, w, dist);
+      d_aw[gs] = s_datt[warp][s];
+      const float aw = s_aw[warp][s];
+      float dp[4], wdp = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { dp[j] = aw * s_dot[warp][s * 4 + j]; wdp = fmaf(w[j], dp[j], wdp); }
+      float dsx = 0.f, dsy = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float ds = w[j] * (dp[j] - wdp);
+        dpow += ds * (-dist[j]);
+        const float dd2 = (ds * (-P)) / (2.f * dist[j]);
+        const int id = s_idx[warp][s * 4 + j];
+        const float ex = sx - kvb[2 * id], ey = sy - kvb[2 * id + 1];
+        dsx = fmaf(ex, dd2, dsx);
+        dsy = fmaf(ey, dd2, dsy);
+        red_add(dkvb + 2 * id, -2.f * ex * dd2);
+        red_add(dkvb + 2 * id + 1, -2.f * ey * dd2);
+      }
+      dsx *= 2.f;
+      dsy *= 2.f;
+      d_off[2 * gs] = dsx;
+      d_off[2 * gs + 1] = dsy;
+      gqx += dsx;
+      gqy += dsy;
+    }
+    gqx = warp_sum(gqx);
+    gqy = warp_sum(gqy);
+    if (lane == 0) {
+      red_add(d_qpos + 2 * gq, gqx);
+      red_add(d_qpos + 2 * gq + 1, gqy);
+    }
+    __syncwarp();
+  }
+  dpow = warp_sum(dpow);
+  if (lane == 0) s_pow[warp] = dpow;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < DK_WARPS; ++i) t += s_pow[i];
+    atomicAdd(d_power, t);
+  }
+}
+
+static int check_deform(int64_t B, int64_t Nq, int64_t Nkv, int64_t H, int64_t C) {
+  AFFB_REQUIRE(B >= 0 && Nq >= 0 && Nkv >= 1 && H >= 1 && C >= 1, "deform_knn: invalid sizes");
+  AFFB_REQUIRE(H * 4 <= DK_SMAX, "deform_knn: at most %d heads supported (got %lld)", DK_SMAX / 4,
+               (long long)H);
+  AFFB_REQUIRE(C % 8 == 0, "deform_knn: channels per head must be a multiple of 8 (got %lld)",
+               (long long)C);
+  AFFB_REQUIRE(Nkv < (1ll << 31) && B < 65536, "deform_knn: size too large");
+  return AFFB_OK;
+}
+
+}  // namespace affb
+
+using namespace affb;
+
+extern "C" int64_t affb_deform_workspace_bytes(int64_t B, int64_t Nkv) {
+  return grid_layout(B, Nkv).total;
+}
+
+extern "C" int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos,
+                                   const float* offsets, const float* attn_w, const void* values,
+                                   const float* power, int dtype, int64_t B, int64_t Nq,
+                                   int64_t Nkv, int64_t H, int64_t C, void* out,
+                                   int32_t* knn_idx, float* knn_d2, void* workspace,
+                                   void* stream) {
+  if (int e = check_deform(B, Nq, Nkv, H, C)) return e;
+  AFFB_REQUIRE(((uintptr_t)workspace & 255) == 0, "deform_knn: workspace must be 256-byte aligned");
+  AFFB_REQUIRE(((uintptr_t)values & 15) == 0 && ((uintptr_t)out & 15) == 0 &&
+                   ((uintptr_t)knn_idx & 15) == 0 && ((uintptr_t)knn_d2 & 15) == 0,
+               "deform_knn: values/out/knn buffers must be 16-byte aligned");
+  if (B == 0 || Nq == 0) return AFFB_OK;
+  cudaStream_t st = as_stream(stream);
+  GridView gv;
+  if (int e = build_grid(kv_pos, B, Nkv, workspace, gv, st)) return e;
+  const unsigned nb = (unsigned)((B * Nq + DK_WARPS - 1) / DK_WARPS);
+  AFFB_DISPATCH(dtype, T,
+                deform_knn_fwd_kernel<T><<<nb, DK_WARPS * 32, 0, st>>>(
+                    query_pos, offsets, attn_w, (const T*)values, power, B, Nq, Nkv, (int)H,
+                    (int)C, gv, (T*)out, knn_idx, knn_d2));
+  AFFB_LAUNCH_CHECK("affb_deform_knn_fwd");
+  return AFFB_OK;
+}
+
+extern "C" int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos,
+                                   const float* offsets, const float* attn_w, const void* values,
+                                   const float* power, const int32_t* knn_idx,
+                                   const float* knn_d2, const void* dout, int dtype, int64_t B,
+                                   int64_t Nq, int64_t Nkv, int64_t H, int64_t C,
+                                   float* d_offsets, float* d_attn_w, float* d_qpos,
+                                   float* d_kvpos, float* d_values_acc, float* d_power,
+                                   void* stream) {
+  if (int e = check_deform(B, Nq, Nkv, H, C)) return e;
+  AFFB_REQUIRE(((uintptr_t)values & 15) == 0 && ((uintptr_t)dout & 15) == 0 &&
+                   ((uintptr_t)d_values_acc & 15) == 0,
+               "deform_knn_bwd: values/dout/d_values must be 16-byte aligned");
+  if (B == 0 || Nq == 0) return AFFB_OK;
+  cudaStream_t st = as_stream(stream);
+  const int64_t need = (B * Nq + DK_WARPS - 1) / DK_WARPS;
+  const unsigned nb = (unsigned)imin64(need, (int64_t)sm_count() * 8);
+  AFFB_DISPATCH(dtype, T,
+                deform_knn_bwd_kernel<T><<<nb, DK_WARPS * 32, 0, st>>>(
+                    query_pos, kv_pos, offsets, attn_w, (const T*)values, power, knn_idx, knn_d2,
+                    (const T*)dout, B, Nq, Nkv, (int)H, (int)C, d_offsets, d_attn_w, d_qpos,
+                    d_kvpos, d_values_acc, d_power));
+  AFFB_LAUNCH_CHECK("affb_deform_knn_bwd");
+  return AFFB_OK;
+}

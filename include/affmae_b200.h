@@ -1,0 +1,199 @@
+/*
+ * affmae_b200 — C ABI of the B200 (sm_100a) kernels that replace AFFMAE's
+ * custom-kernel hot path (the Triton operators of src/layers/kernels/ in
+ * najafian-lab/affmae).
+ *
+ * Conventions shared by every entry point
+ *  - All tensor arguments are device pointers to dense, row-major
+ *    (C-contiguous) arrays whose shapes are given in the comment of each
+ *    function.  Pointers must be 16-byte aligned where a function says so.
+ *  - `dtype` is one of AFFB_F32 / AFFB_F16 / AFFB_BF16 and names the storage
+ *    type of the tensors documented as "T".  Arithmetic is fp32 throughout.
+ *  - `stream` is a cudaStream_t passed as void*.  Work is only enqueued;
+ *    no entry point synchronises the host or allocates device memory.
+ *  - Buffers documented as "fp32 accumulator, zeroed by the caller" receive
+ *    atomic scatter-adds; the caller clears them before the call.
+ *  - Return value: AFFB_OK, or an error code with a message available from
+ *    affb_last_error() (thread-local).  Shape/argument errors are detected
+ *    before anything is enqueued.
+ *
+ * Each declaration cites the reference interface it replaces as
+ * file:line inside the reference repository.
+ */
+#ifndef AFFMAE_B200_H_
+#define AFFMAE_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { AFFB_F32 = 0, AFFB_F16 = 1, AFFB_BF16 = 2 };
+enum { AFFB_OK = 0, AFFB_ERR_INVALID = 1, AFFB_ERR_CUDA = 2 };
+
+/* Last error message of the calling thread ("" if none). */
+const char* affb_last_error(void);
+/* ABI version, bumped on any signature change. */
+int affb_abi_version(void);
+
+/* ------------------------------------------------------------------ KNN --
+ * Replaces knn() / KNNFunction / knn_forward
+ * (src/layers/kernels/knn.py:1615, :1543, :1368) and the K>8 fallback
+ * knn_pytorch_large (knn.py:1312) with one exact kernel for every K.
+ * query [B,M,D] T, ref [B,N,D] T, D in {2,3,4}, 1 <= K <= min(N, 256).
+ * out_idx [B,M,K] int64: indices of the K nearest refs by fp32 squared
+ * Euclidean distance (products and sums rounded separately, no FMA),
+ * ascending, ties broken by lower index.                                   */
+int affb_knn(const void* query, const void* ref, int dtype, int64_t B, int64_t M,
+             int64_t N, int D, int K, int64_t* out_idx, void* stream);
+
+/* -------------------------------------------------- weighted features --
+ * Replaces WeightedFeaturesFunction (src/layers/kernels/weighted_features.py:401)
+ * and, with IC = 1, WeightedGatherFunction (weighted_gather.py:329).
+ * out[b,i,ic,c] = sum_m w[b,i,m,ic] * feat[b, idx[b,i,m], c]
+ * w [B,No,M,IC] T, feat [B,N,C] T, idx [B,No,M] int32, out [B,No,IC,C] T.  */
+int affb_weighted_features_fwd(const void* w, const void* feat, const int32_t* idx, int dtype,
+                               int64_t B, int64_t No, int64_t M, int64_t IC, int64_t N,
+                               int64_t C, void* out, void* stream);
+/* Backward (weighted_features.py:164-345, weighted_gather.py:127-276):
+ * dw [B,No,M,IC] T (written), dfeat_acc [B,N,C] fp32 accumulator zeroed by
+ * the caller (scatter-added).                                              */
+int affb_weighted_features_bwd(const void* dout, const void* w, const void* feat,
+                               const int32_t* idx, int dtype, int64_t B, int64_t No,
+                               int64_t M, int64_t IC, int64_t N, int64_t C, void* dw,
+                               float* dfeat_acc, void* stream);
+
+/* ------------------------------------------- neighbourhood attention --
+ * Replaces launch_flash_nbhood_attn_fwd (src/layers/kernels/local_attn.py:609)
+ * i.e. the forward of FlashLocalAttentionFunction (local_attn.py:843).
+ * q,k,v [B,H,N,D] T (D % 8 == 0, D <= 256, 16-byte aligned);
+ * member_idx [B,N,M] int32 (M % 8 == 0); bias [B,H,N,M] T or NULL;
+ * mask [B,mask_heads,N,M] uint8 (nonzero = attend) or NULL, mask_heads in {1,H};
+ * blank_k, blank_v [H,D] T or NULL (both or neither);
+ * out [B,H,N,D] T; lse [B,H,N] fp32.                                       */
+int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v, const int32_t* member_idx,
+                       const void* bias, const uint8_t* mask, int mask_heads,
+                       const void* blank_k, const void* blank_v, int dtype, int64_t B,
+                       int64_t H, int64_t N, int64_t D, int64_t M, float scale, void* out,
+                       float* lse, void* stream);
+/* Replaces launch_flash_nbhood_attn_bwd (local_attn.py:711).
+ * o, dout [B,H,N,D] T; lse [B,H,N] fp32 from the forward.
+ * dq [B,H,N,D] T (written); dk_acc, dv_acc [B,H,N,D] fp32 accumulators
+ * zeroed by the caller; dbias [B,H,N,M] T (written) or NULL when bias is
+ * NULL; dbk_acc, dbv_acc [H,D] fp32 accumulators zeroed by the caller, or
+ * NULL when there is no blank token.                                       */
+int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                       const void* dout, const float* lse, const int32_t* member_idx,
+                       const void* bias, const uint8_t* mask, int mask_heads,
+                       const void* blank_k, const void* blank_v, int dtype, int64_t B,
+                       int64_t H, int64_t N, int64_t D, int64_t M, float scale, void* dq,
+                       float* dk_acc, float* dv_acc, void* dbias, float* dbk_acc,
+                       float* dbv_acc, void* stream);
+
+/* ------------------------------------------------ relative-position bias --
+ * Replaces the gather of ClusterAttention._make_pos_bias
+ * (src/layers/attention.py:110-124):
+ * out[b,h,n,m] = table[pe_idx[b,n,m], h]; table [T,H] T, pe_idx [B,N,M] int64,
+ * out [B,H,N,M] T.                                                          */
+int affb_pos_bias_fwd(const void* table, const int64_t* pe_idx, int dtype, int64_t T,
+                      int64_t H, int64_t B, int64_t N, int64_t M, void* out, void* stream);
+/* dtable_acc [T,H] fp32 accumulator zeroed by the caller.                  */
+int affb_pos_bias_bwd(const void* dbias, const int64_t* pe_idx, int dtype, int64_t T,
+                      int64_t H, int64_t B, int64_t N, int64_t M, float* dtable_acc,
+                      void* stream);
+
+/* --------------------------------- fused KNN deformable attention (2-D) --
+ * Replaces fused_knn_deform_cross_attn_forward_save
+ * (src/layers/kernels/fused_deform_attn.py:2592) and, with kv_pos == query_pos
+ * and Nkv == Nq, fused_knn_deform_self_attn_forward_save (:2530).
+ * query_pos [B,Nq,2] fp32, kv_pos [B,Nkv,2] fp32, offsets [B,Nq,H,4,2] fp32,
+ * attn_w [B,Nq,H,4] fp32, values [B,Nkv,H,C] T (C % 8 == 0, H <= 16),
+ * power: 1 fp32 on device (clamped to >= 1e-6 on device).  For every
+ * (query, head, point) the sample s = query_pos + offset; its 4 nearest kv
+ * positions (fp32 squared distance, ties -> lower index) get Shepard weights
+ * softmax(-P*(sqrt(d2)+1e-6)) with +1e-8 in the denominator;
+ * out [B,Nq,H,C] T = sum_p attn_w * sum_j w_j v_j.
+ * knn_idx [B,Nq,H,4,4] int32 and knn_d2 [B,Nq,H,4,4] fp32 are written for the
+ * backward.  `workspace` (device, affb_deform_workspace_bytes(B,Nkv) bytes,
+ * 256-byte aligned) receives the spatial grid of kv_pos built by this call. */
+int64_t affb_deform_workspace_bytes(int64_t B, int64_t Nkv);
+int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos, const float* offsets,
+                        const float* attn_w, const void* values, const float* power,
+                        int dtype, int64_t B, int64_t Nq, int64_t Nkv, int64_t H, int64_t C,
+                        void* out, int32_t* knn_idx, float* knn_d2, void* workspace,
+                        void* stream);
+/* Replaces fused_knn_deform_cross_attn_backward (fused_deform_attn.py:2792)
+ * and fused_knn_deform_self_attn_backward (:2661).  dout [B,Nq,H,C] T.
+ * Written: d_offsets [B,Nq,H,4,2] fp32, d_attn_w [B,Nq,H,4] fp32.
+ * Accumulated (zeroed by the caller): d_qpos [B,Nq,2] fp32,
+ * d_kvpos [B,Nkv,2] fp32 (may alias d_qpos for self-attention),
+ * d_values_acc [B,Nkv,H,C] fp32, d_power [1] fp32.                          */
+int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos, const float* offsets,
+                        const float* attn_w, const void* values, const float* power,
+                        const int32_t* knn_idx, const float* knn_d2, const void* dout,
+                        int dtype, int64_t B, int64_t Nq, int64_t Nkv, int64_t H, int64_t C,
+                        float* d_offsets, float* d_attn_w, float* d_qpos, float* d_kvpos,
+                        float* d_values_acc, float* d_power, void* stream);
+
+/* ------------------------ deformable attention with given neighbours --
+ * Replaces fused_deform_attn_forward / _backward
+ * (src/layers/kernels/fused_deform_attn.py:502-640).
+ * sl [B,N,D] fp32, kv_pos [B,Nkv,D] fp32, nb_idx [B,N,K] int32 (K <= 16),
+ * power 1 fp32 on device, attn_w [B,N] fp32, values [B,Nkv,C] T,
+ * out [B,N,C] T = attn_w * sum_k softmax_k(-P*(sqrt(d2)+1e-6)) values[nb].  */
+int affb_deform_nbidx_fwd(const float* sl, const float* kv_pos, const int32_t* nb_idx,
+                          const float* power, const float* attn_w, const void* values,
+                          int dtype, int64_t B, int64_t N, int64_t Nkv, int64_t K, int D,
+                          int64_t C, void* out, void* stream);
+/* Written: d_sl [B,N,D] fp32, d_attn_w [B,N] fp32.  Accumulated (zeroed by
+ * the caller): d_kvpos [B,Nkv,D] fp32, d_power [1] fp32, d_values_acc
+ * [B,Nkv,C] fp32.                                                          */
+int affb_deform_nbidx_bwd(const float* sl, const float* kv_pos, const int32_t* nb_idx,
+                          const float* power, const float* attn_w, const void* values,
+                          const void* dout, int dtype, int64_t B, int64_t N, int64_t Nkv,
+                          int64_t K, int D, int64_t C, float* d_sl, float* d_kvpos,
+                          float* d_power, float* d_attn_w, float* d_values_acc,
+                          void* stream);
+
+/* ------------------------------------------------------------ MSDETRPC --
+ * Replaces MSDETRPCFunction (src/layers/kernels/msdetrpc.py:372).
+ * out[b,n,c] = sum_m attn[b,n,m] * sum_k w[b,n,m,k] * val[b, idx[b,n,m,k], c]
+ * idx [B,N,M,K] int32, w [B,N,M,K] T, attn [B,N,M] T, val [B,Nv,C] T,
+ * out [B,N,C] T.                                                            */
+int affb_msdetrpc_fwd(const int32_t* idx, const void* w, const void* attn, const void* val,
+                      int dtype, int64_t B, int64_t N, int64_t M, int64_t K, int64_t Nv,
+                      int64_t C, void* out, void* stream);
+/* dw [B,N,M,K] T and dattn [B,N,M] T written; dval_acc [B,Nv,C] fp32
+ * accumulator zeroed by the caller.                                        */
+int affb_msdetrpc_bwd(const void* dout, const int32_t* idx, const void* w, const void* attn,
+                      const void* val, int dtype, int64_t B, int64_t N, int64_t M, int64_t K,
+                      int64_t Nv, int64_t C, void* dw, void* dattn, float* dval_acc,
+                      void* stream);
+
+/* ------------------------------------------------------------ MSSample --
+ * Replaces MSSampleFunction (src/layers/kernels/mssample.py:402).
+ * sl [B,N,D] fp32, kv_pos [B,Nkv,D] fp32, nb_idx [B,N,K] int32 (K <= 16),
+ * power 1 fp32 on device; w_out [B,N,K] fp32 =
+ * softmax_k(-P*sqrt(d2+1e-6)) with +1e-8 in the denominator.               */
+int affb_mssample_fwd(const float* sl, const float* kv_pos, const int32_t* nb_idx,
+                      const float* power, int64_t B, int64_t N, int64_t Nkv, int64_t K, int D,
+                      float* w_out, void* stream);
+/* dw [B,N,K] fp32 upstream gradient; w the forward output.  Written: d_sl
+ * [B,N,D] fp32.  Accumulated (zeroed by the caller): d_kvpos [B,Nkv,D],
+ * d_power [1].                                                              */
+int affb_mssample_bwd(const float* dw, const float* sl, const float* kv_pos,
+                      const int32_t* nb_idx, const float* power, const float* w, int64_t B,
+                      int64_t N, int64_t Nkv, int64_t K, int D, float* d_sl, float* d_kvpos,
+                      float* d_power, void* stream);
+
+/* ----------------------------------------------------------- utilities --
+ * dst[i] = (T) src[i] for n elements (fp32 accumulator -> storage dtype).
+ * No counterpart in the reference (it casts with torch's .to()).           */
+int affb_cast_f32(const float* src, void* dst, int dtype, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AFFMAE_B200_H_ */

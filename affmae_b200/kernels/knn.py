@@ -1,0 +1,78 @@
+"""K-nearest neighbours over 2/3/4-D points (mirrors src/layers/kernels/knn.py).
+
+Public API as in the reference: ``knn`` (knn.py:1615), ``knn_triton``
+(:1585), ``KNNFunction`` (:1543) and ``knn_forward`` (:1368).  One exact
+CUDA kernel serves every K (the reference switches to cdist+topk for K > 8):
+fp32 squared distances with separately rounded products and sums, ascending,
+ties broken by the lower index.
+"""
+from __future__ import annotations
+
+import torch
+from torch.autograd import Function
+from torch.amp import custom_fwd
+
+from .. import _native as nat
+
+
+def _check(query, ref, k, D):
+    nat.require_cuda(query, ref)
+    assert query.dim() == 3 and ref.dim() == 3, "Expected 3D tensors [B, N, D]"
+    assert query.shape[0] == ref.shape[0], "Batch sizes must match"
+    assert query.shape[2] == ref.shape[2] == D, \
+        f"Expected D={D}, got query D={query.shape[2]}, ref D={ref.shape[2]}"
+    assert D in [2, 3, 4], f"D must be 2, 3, or 4, got {D}"
+    assert k <= ref.shape[1], f"k={k} exceeds number of reference points N={ref.shape[1]}"
+
+
+def _knn_int64(query, ref, k, D):
+    if query.dtype != ref.dtype or query.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        query, ref = query.float(), ref.float()
+    query = query.contiguous()
+    ref = ref.contiguous()
+    B, M, _ = query.shape
+    N = ref.shape[1]
+    out = torch.empty((B, M, k), dtype=torch.int64, device=query.device)
+    nat.call("affb_knn", nat.ptr(query), nat.ptr(ref), nat.dcode(query), B, M, N, D, int(k),
+             nat.ptr(out), nat.stream(query.device))
+    return out
+
+
+def knn_forward(query, ref, k, D=2, use_v2=True, use_heuristic=True):
+    """Indices [B, M, k] (int32) of the k nearest ``ref`` points of each query."""
+    _check(query, ref, k, D)
+    return _knn_int64(query, ref, k, D).to(torch.int32)
+
+
+class KNNFunction(Function):
+    """Forward-only autograd Function (KNN indices carry no gradient)."""
+
+    @staticmethod
+    @custom_fwd(device_type="cuda")
+    def forward(ctx, query, ref, k, D=2):
+        with torch.no_grad():
+            q, r = query.detach(), ref.detach()
+            _check(q, r, k, D)
+            return _knn_int64(q, r, k, D)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        return None, None, None, None
+
+
+def knn_triton(query, ref, k, D=2):
+    """Same contract as the reference's ``knn_triton``: int64 indices [B, M, k]."""
+    return KNNFunction.apply(query, ref, k, D)
+
+
+def knn(query, database, k, return_dist=False, D=None):
+    """knn_keops-compatible entry point; optionally also returns squared distances."""
+    if D is None:
+        D = query.shape[-1]
+    indices = knn_triton(query, database, k, D=D)
+    if return_dist:
+        B, M, K = indices.shape
+        nbr = database.gather(dim=1, index=indices.view(B, M * K, 1).expand(-1, -1, D)).view(B, M, K, D)
+        distances = ((query.unsqueeze(2) - nbr) ** 2).sum(dim=-1)
+        return indices, distances
+    return indices

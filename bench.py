@@ -1,0 +1,356 @@
+"""Benchmark: neighbourhood (cluster) attention forward + backward on B200.
+
+Workload: bf16, B=32 images, N=4608 visible tokens (0.5
+mask of a 96x96 grid), clusters of 8 queries attending the 48 members of their
+6 nearest clusters, 4 heads x d=32, relative-position bias [B,H,N,M], blank
+token.  One step = one forward + one backward call of the hot path.
+
+  value : algorithmic bytes of fwd+bwd (interface bytes: inputs read once,
+          outputs written once) / device time, inputs resident in HBM, L2
+          flushed (256 MiB write) before every step outside the timed events.
+  e2e   : the same bytes / time of the public autograd path
+          (FlashLocalAttentionFunction.apply + backward) including the
+          host->device copies of all inputs from pinned memory and the
+          device->host copies of the output and all gradients.
+
+Multi-GPU: the op has no exchange step, so N GPUs run N independent replicas
+(weak scaling); value is summed over ranks using the max time over ranks.
+
+``--impl reference`` times the reference's pure-PyTorch formula of this op
+(the gathered-softmax formula of local_attn.py:979-1006, autograd backward)
+on the host cores on a bounded sample (one image per step).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "nbr-attn fwd+bwd HBM GB/s"
+CFG = dict(B=32, side=96, keep=0.5, H=4, d=32, nbhd=48)
+
+
+def workload_config(extra=None):
+    c = {"workload": "neighbourhood attention fwd+bwd (config 3)", "global_batch": CFG["B"],
+         "tokens": int(CFG["side"] ** 2 * CFG["keep"]), "heads": CFG["H"], "head_dim": CFG["d"],
+         "neighbours": CFG["nbhd"], "bias": True, "blank": True, "mask": None,
+         "l2": "flushed by a 256 MiB write before every timed step"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------- helpers --
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        dist.init_process_group(backend=backend)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda" if torch.cuda.is_available() else "cpu", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------ CPU baseline --
+def cpu_reference_step(inp_cpu, threads):
+    """The reference's PyTorch formula (local_attn.py:979-1006) on one image, fp32,
+    forward + autograd backward.  Returns seconds."""
+    import oracle
+    torch.set_num_threads(threads)
+    leaves = {n: inp_cpu[n].float().requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
+    t0 = time.perf_counter()
+    out = oracle.nbhd_attn_formula(leaves["q"], leaves["k"], leaves["v"], inp_cpu["member_idx"],
+                                   inp_cpu["scale"], bias=leaves["bias"], blank_k=leaves["blank_k"],
+                                   blank_v=leaves["blank_v"])
+    out.backward(inp_cpu["dout"].float())
+    return time.perf_counter() - t0
+
+
+def cpu_sample(inp, b=1):
+    """First `b` images of the workload, on the host."""
+    out = {}
+    for k, v in inp.items():
+        if torch.is_tensor(v) and v.dim() >= 3:
+            out[k] = v[:b].detach().cpu()
+        elif torch.is_tensor(v):
+            out[k] = v.detach().cpu()
+        else:
+            out[k] = v
+    return out
+
+
+def bytes_for(B):
+    from affmae_b200.workloads import nbhd_attention_bytes
+    N = int(CFG["side"] ** 2 * CFG["keep"])
+    f, b = nbhd_attention_bytes(B, CFG["H"], N, CFG["d"], CFG["nbhd"])
+    return f, b
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from affmae_b200.workloads import nbhd_attention_inputs
+    threads = os.cpu_count() or 1
+    inp = nbhd_attention_inputs(B=1, dtype=torch.float32, device="cpu",
+                                **{k: CFG[k] for k in ("side", "keep", "H", "d", "nbhd")})
+    inp = cpu_sample(inp, 1)
+    f, b = bytes_for(1)
+    for _ in range(args.warmup):
+        cpu_reference_step(inp, threads)
+    ts = [cpu_reference_step(inp, threads) for _ in range(args.steps)]
+    t = sum(ts) / len(ts)
+    value = (f + b) / t / 1e9
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config({"sample": "1 of 32 images per step"}), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": "1 image (1/32 of the batch) per step, reference PyTorch formula, fp32"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ GPU arm --
+def run_gpu(args, world, rank, local):
+    from affmae_b200 import _native as nat
+    from affmae_b200.workloads import nbhd_attention_inputs
+    from affmae_b200.kernels.local_attn import (FlashLocalAttentionFunction, launch_flash_nbhood_attn_bwd,
+                                                launch_flash_nbhood_attn_fwd)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    nat.lib()
+    inp = nbhd_attention_inputs(B=CFG["B"], dtype=torch.bfloat16, seed=rank, device=dev,
+                                **{k: CFG[k] for k in ("side", "keep", "H", "d", "nbhd")})
+    q, k, v, mi, bias = inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["bias"]
+    bk, bv, do, scale = inp["blank_k"], inp["blank_v"], inp["dout"], inp["scale"]
+    fwd_bytes, bwd_bytes = bytes_for(CFG["B"])
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        o, lse = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, bias=bias, blank_k=bk, blank_v=bv)
+        if ev is not None:
+            ev[0].record(stream)
+        g = launch_flash_nbhood_attn_bwd(q, k, v, mi, scale, o, lse, do, bias=bias, blank_k=bk, blank_v=bv)
+        if ev is not None:
+            ev[1].record(stream)
+        return o, g
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- device-timed value: per-step events, L2 flushed before each step
+    times, fwd_t, bwd_t = [], [], []
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            ef = torch.cuda.Event(enable_timing=True)
+            eb0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step((ef, e1))
+            times.append((e0, ef, e1))
+        torch.cuda.synchronize()
+        # kernel-only bwd timing (the dominant kernel): events around the C call
+        o, lse = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, bias=bias, blank_k=bk, blank_v=bv)
+        dk_acc = torch.zeros(q.shape, device=dev, dtype=torch.float32)
+        dv_acc = torch.zeros(q.shape, device=dev, dtype=torch.float32)
+        dq = torch.empty_like(q)
+        dbias = torch.empty_like(bias)
+        dbk = torch.zeros(bk.shape, device=dev, dtype=torch.float32)
+        dbv = torch.zeros(bv.shape, device=dev, dtype=torch.float32)
+        kern_ms = []
+        B, H, N, D = q.shape
+        for _ in range(args.steps):
+            flush.fill_(1)
+            dk_acc.zero_(); dv_acc.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            c = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            nat.call("affb_nbhd_attn_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
+                     lse.data_ptr(), mi.data_ptr(), bias.data_ptr(), None, 1, bk.data_ptr(), bv.data_ptr(),
+                     nat.BF16, B, H, N, D, CFG["nbhd"], float(scale), dq.data_ptr(), dk_acc.data_ptr(),
+                     dv_acc.data_ptr(), dbias.data_ptr(), dbk.data_ptr(), dbv.data_ptr(), stream.cuda_stream)
+            c.record(stream)
+            kern_ms.append((a, c))
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    step_ms = [a.elapsed_time(c) for a, _, c in times]
+    f_ms = [a.elapsed_time(f) for a, f, _ in times]
+    b_ms = [f.elapsed_time(c) for _, f, c in times]
+    total_s = sum(step_ms) / 1e3
+    total_s = max_over_ranks(total_s, world)
+    value = world * args.steps * (fwd_bytes + bwd_bytes) / total_s / 1e9
+    kbwd = sum(a.elapsed_time(c) for a, c in kern_ms) / len(kern_ms)
+    peak, peak_kind = measured_peaks()
+    achieved = bwd_bytes / (kbwd / 1e3) / 1e9
+
+    # ---- e2e through the public autograd API with host buffers
+    host = {n: inp[n].detach().cpu().pin_memory() for n in ("q", "k", "v", "member_idx", "bias", "blank_k",
+                                                             "blank_v", "dout")}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    outs_host = None
+
+    def e2e_step():
+        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
+        leaves = {n: d[n].requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
+        out = FlashLocalAttentionFunction.apply(leaves["q"], leaves["k"], leaves["v"], d["member_idx"],
+                                                leaves["bias"], None, leaves["blank_k"], leaves["blank_v"], scale)
+        out.backward(d["dout"])
+        res = [out.detach()] + [leaves[n].grad for n in ("q", "k", "v", "bias", "blank_k", "blank_v")]
+        return [r.to("cpu", non_blocking=True) for r in res]
+
+    for _ in range(max(1, args.warmup)):
+        outs_host = e2e_step()
+    torch.cuda.synchronize()
+    d2h = sum(t.numel() * t.element_size() for t in outs_host)
+    barrier(world)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    c = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        outs_host = e2e_step()
+    c.record(stream)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(a.elapsed_time(c) / 1e3, world)
+    e2e_value = world * args.steps * (fwd_bytes + bwd_bytes) / e2e_s / 1e9
+
+    # ---- CPU baseline (rank 0, N=1 only): reference formula on one image
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        sample = cpu_sample({k2: (v2.float() if torch.is_tensor(v2) and v2.is_floating_point() else v2)
+                             for k2, v2 in inp.items()}, 1)
+        cpu_reference_step(sample, threads)
+        ts = [cpu_reference_step(sample, threads) for _ in range(3)]
+        f1, b1 = bytes_for(1)
+        cpu = {"value": (f1 + b1) / (sum(ts) / len(ts)) / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": "1 image (1/32 of the batch), reference PyTorch formula fwd+autograd bwd, fp32, 3 runs"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": workload_config({"parallelism": f"replicas x{world}" if world > 1 else "single GPU"}),
+                "fwd_ms": statistics.median(f_ms), "bwd_ms": statistics.median(b_ms),
+                "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "ms_per_step": e2e_s * 1e3 / args.steps},
+                "roofline": {"kernel": "nbhd_attn_bwd_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                             "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                             "algorithmic_bytes": bwd_bytes, "kernel_ms": kbwd},
+                "cpu_baseline": cpu, "clocks": clocks,
+                "gpu_launches": args.steps * 4}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_gpu(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

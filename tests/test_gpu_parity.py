@@ -1,0 +1,365 @@
+"""Parity of the CUDA operators (through the C ABI) with the CPU oracle and the
+reference's golden vectors.
+
+Tolerances (relative error = max|a-b| / max|b| per tensor):
+  KNN indices: bit-exact;  fp32 forward: 1e-5;  atomics-based backward: 1e-4;
+  bf16/fp16 inputs: 2e-2 against the oracle evaluated on the rounded inputs.
+The reference stores the local-attention output through fp16
+(local_attn.py:340), so its golden O is compared at 2e-3.
+"""
+import pytest
+import torch
+
+import oracle
+from conftest import golden, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32, TOL_BWD, TOL_LP = 1e-5, 1e-4, 2e-2
+
+
+def dev(t, device, dtype=None):
+    t = t.to(device)
+    return t.to(dtype) if dtype is not None else t
+
+
+# ----------------------------------------------------------------------- KNN
+@pytest.mark.parametrize("tag", ["d2_k4", "d2_k8_grid", "d3_k6", "d2_k3_grid"])
+def test_knn_golden(cuda, tag):
+    from affmae_b200.kernels.knn import knn
+    g = golden(f"knn_{tag}")
+    idx = knn(dev(g["query"], cuda), dev(g["ref"], cuda), int(g["k"]))
+    assert idx.dtype == torch.int64
+    assert torch.equal(idx.cpu(), g["idx"])
+
+
+@pytest.mark.parametrize("K", [1, 6, 16, 33, 48, 100, 256])
+@pytest.mark.parametrize("D", [2, 3, 4])
+def test_knn_random_exact(cuda, K, D):
+    from affmae_b200.kernels.knn import knn
+    gen = torch.Generator().manual_seed(K * 10 + D)
+    q = torch.rand((2, 301, D), generator=gen) * 50
+    r = torch.rand((2, 2600, D), generator=gen) * 50
+    idx = knn(q.to(cuda), r.to(cuda), K)
+    assert torch.equal(idx.cpu(), oracle.knn(q, r, K))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_knn_ties_and_low_precision(cuda, dtype):
+    from affmae_b200.kernels.knn import knn
+    gen = torch.Generator().manual_seed(7)
+    q = torch.randint(0, 20, (3, 200, 2), generator=gen).to(dtype)
+    r = torch.randint(0, 20, (3, 500, 2), generator=gen).to(dtype)
+    idx = knn(q.to(cuda), r.to(cuda), 48)
+    assert torch.equal(idx.cpu(), oracle.knn(q.float(), r.float(), 48))
+
+
+def test_knn_baseline_config_sweep(cuda):
+    """Config 2 shapes: 96x96 stride-4 lattice jittered, B=8, N=2304 (self and 0.25N queries)."""
+    from affmae_b200.kernels.knn import knn
+    gen = torch.Generator().manual_seed(0)
+    ys, xs = torch.meshgrid(torch.arange(48.), torch.arange(48.), indexing="ij")
+    grid = torch.stack([xs, ys], -1).reshape(1, -1, 2) * 2
+    pos = (grid + torch.rand((8, grid.shape[1], 2), generator=gen) - 0.5).float()
+    for K in (16, 48):
+        idx = knn(pos.to(cuda), pos.to(cuda), K)
+        assert torch.equal(idx.cpu(), oracle.knn(pos, pos, K))
+        qd = pos[:, : pos.shape[1] // 4]
+        idx = knn(qd.to(cuda), pos.to(cuda), K)
+        assert torch.equal(idx.cpu(), oracle.knn(qd, pos, K))
+
+
+def test_knn_errors(cuda):
+    from affmae_b200.kernels.knn import knn
+    q = torch.rand((1, 4, 2), device=cuda)
+    with pytest.raises(AssertionError):
+        knn(q, q, 5)
+
+
+# ------------------------------------------------------- neighbourhood attention
+def _attn_inputs(B, H, N, D, M, dtype, mask=True, blank=True, bias=True, seed=0, cuda=None):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn((B, H, N, D), generator=gen) / D ** 0.5
+    k = torch.randn((B, H, N, D), generator=gen) / D ** 0.5
+    v = torch.randn((B, H, N, D), generator=gen) / D ** 0.5
+    mi = torch.randint(0, N, (B, N, M), generator=gen, dtype=torch.int32)
+    b = torch.randn((B, H, N, M), generator=gen) * 0.5 if bias else None
+    m = (torch.rand((B, 1, N, M), generator=gen) > 0.2) if mask else None
+    bk = torch.randn((H, D), generator=gen) * 0.2 if blank else None
+    bv = torch.randn((H, D), generator=gen) * 0.2 if blank else None
+    do = torch.randn((B, H, N, D), generator=gen)
+    cast = lambda t: None if t is None else t.to(dtype)
+    return dict(q=cast(q), k=cast(k), v=cast(v), mi=mi, bias=cast(b), mask=m, blank_k=cast(bk),
+                blank_v=cast(bv), do=cast(do))
+
+
+def _to(d, device):
+    return {k: (None if v is None else v.to(device)) for k, v in d.items()}
+
+
+@pytest.mark.parametrize("tag", ["full", "plain", "m24"])
+def test_local_attn_golden(cuda, tag):
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    g = golden(f"local_attn_{tag}")
+    G = _to(g, cuda)
+    kw = dict(bias=G.get("bias"), mask=G.get("mask"), blank_k=G.get("blank_k"), blank_v=G.get("blank_v"))
+    scale = float(g["scale"])
+    o, lse = launch_flash_nbhood_attn_fwd(G["q"], G["k"], G["v"], G["mi"], scale, **kw)
+    assert rel_err(lse.cpu(), g["lse"]) < TOL_F32
+    assert rel_err(o.cpu(), g["o"]) < 2e-3
+    okw = dict(bias=g.get("bias"), mask=g.get("mask"), blank_k=g.get("blank_k"), blank_v=g.get("blank_v"))
+    o_ref, _ = oracle.nbhd_attn_fwd(g["q"], g["k"], g["v"], g["mi"], scale, **okw)
+    assert rel_err(o.cpu(), o_ref) < TOL_F32
+    # backward from the reference's stored O (fp16-rounded) reproduces its grads
+    dq, dk, dv, dbias, dbk, dbv = launch_flash_nbhood_attn_bwd(G["q"], G["k"], G["v"], G["mi"], scale,
+                                                               G["o"], G["lse"], G["do"], **kw)
+    for name, a in [("dq", dq), ("dk", dk), ("dv", dv), ("dbias", dbias), ("dbk", dbk), ("dbv", dbv)]:
+        if name in g:
+            assert rel_err(a.cpu(), g[name]) < TOL_BWD, name
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_LP),
+                                       (torch.float16, TOL_LP)])
+@pytest.mark.parametrize("opts", [dict(), dict(mask=False), dict(blank=False, bias=False),
+                                  dict(mask=False, blank=False, bias=False)])
+@pytest.mark.parametrize("shape", [(2, 4, 200, 32, 48), (1, 3, 77, 64, 16), (1, 2, 40, 8, 8),
+                                   (1, 2, 33, 128, 24)])
+def test_local_attn_random(cuda, dtype, tol, opts, shape):
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    B, H, N, D, M = shape
+    inp = _attn_inputs(B, H, N, D, M, dtype, seed=sum(shape), **opts)
+    G = _to(inp, cuda)
+    kw = lambda d: dict(bias=d["bias"], mask=d["mask"], blank_k=d["blank_k"], blank_v=d["blank_v"])
+    scale = D ** -0.5
+    o, lse = launch_flash_nbhood_attn_fwd(G["q"], G["k"], G["v"], G["mi"], scale, **kw(G))
+    assert o.dtype == dtype
+    o_ref, lse_ref = oracle.nbhd_attn_fwd(inp["q"], inp["k"], inp["v"], inp["mi"], scale, **kw(inp))
+    assert rel_err(o.cpu(), o_ref) < tol
+    assert rel_err(lse.cpu(), lse_ref) < max(tol, TOL_F32)
+    grads = launch_flash_nbhood_attn_bwd(G["q"], G["k"], G["v"], G["mi"], scale, o, lse, G["do"], **kw(G))
+    ref = oracle.nbhd_attn_bwd(inp["q"], inp["k"], inp["v"], inp["mi"], scale, o.cpu(), lse.cpu(),
+                               inp["do"], **kw(inp))
+    btol = TOL_BWD if dtype == torch.float32 else TOL_LP
+    for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
+        assert (a is None) == (b is None), name
+        if a is not None:
+            assert a.dtype == dtype
+            assert rel_err(a.cpu(), b) < btol, name
+
+
+def test_local_attn_autograd_function(cuda):
+    from affmae_b200.kernels.local_attn import FlashLocalAttentionFunction
+    inp = _attn_inputs(2, 4, 64, 32, 48, torch.float32, seed=3)
+    G = _to(inp, cuda)
+    leaves = {n: G[n].clone().requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
+    out = FlashLocalAttentionFunction.apply(leaves["q"], leaves["k"], leaves["v"], G["mi"].long(),
+                                            leaves["bias"], G["mask"], leaves["blank_k"],
+                                            leaves["blank_v"], 32 ** -0.5)
+    out.backward(G["do"])
+    ref_leaves = {n: inp[n].double().requires_grad_() for n in leaves}
+    ref = oracle.nbhd_attn_formula(ref_leaves["q"], ref_leaves["k"], ref_leaves["v"], inp["mi"], 32 ** -0.5,
+                                   bias=ref_leaves["bias"], mask=inp["mask"], blank_k=ref_leaves["blank_k"],
+                                   blank_v=ref_leaves["blank_v"])
+    ref.backward(inp["do"].double())
+    assert rel_err(out.detach().cpu(), ref.detach()) < TOL_F32
+    for n in leaves:
+        assert rel_err(leaves[n].grad.cpu(), ref_leaves[n].grad) < TOL_BWD, n
+
+
+# --------------------------------------------------------- weighted features
+def test_weighted_features_golden(cuda):
+    from affmae_b200.kernels.weighted_features import weighted_features_fwd, weighted_features_bwd
+    g = golden("weighted_features")
+    G = _to(g, cuda)
+    assert rel_err(weighted_features_fwd(G["w"], G["feat"], G["idx"]).cpu(), g["out"]) < TOL_F32
+    dw, df = weighted_features_bwd(G["dout"], G["w"], G["feat"], G["idx"])
+    assert rel_err(dw.cpu(), g["dw"]) < TOL_F32
+    assert rel_err(df.cpu(), g["dfeat"]) < TOL_BWD
+
+
+def test_weighted_gather_golden(cuda):
+    from affmae_b200.kernels.weighted_gather import WeightedGatherFunction
+    g = golden("weighted_gather")
+    G = _to(g, cuda)
+    w = G["w"].clone().requires_grad_()
+    f = G["feat"].clone().requires_grad_()
+    out = WeightedGatherFunction.apply(G["idx"], w, f)
+    assert rel_err(out.detach().cpu(), g["out"]) < TOL_F32
+    out.backward(G["dout"])
+    assert rel_err(w.grad.cpu(), g["dw"]) < TOL_F32
+    assert rel_err(f.grad.cpu(), g["dfeat"]) < TOL_BWD
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_LP)])
+@pytest.mark.parametrize("shape", [(2, 300, 48, 4, 700, 96), (2, 100, 48, 1, 4096, 128), (1, 50, 7, 3, 60, 13),
+                                   (1, 20, 40, 9, 30, 24)])
+def test_weighted_features_random(cuda, dtype, tol, shape):
+    from affmae_b200.kernels.weighted_features import weighted_features_fwd, weighted_features_bwd
+    B, No, M, IC, N, C = shape
+    gen = torch.Generator().manual_seed(sum(shape))
+    w = torch.randn((B, No, M, IC), generator=gen).to(dtype)
+    f = torch.randn((B, N, C), generator=gen).to(dtype)
+    idx = torch.randint(0, N, (B, No, M), generator=gen, dtype=torch.int32)
+    do = torch.randn((B, No, IC, C), generator=gen).to(dtype)
+    out = weighted_features_fwd(w.to(cuda), f.to(cuda), idx.to(cuda))
+    assert rel_err(out.cpu(), oracle.weighted_features_fwd(w, f, idx)) < tol
+    dw, df = weighted_features_bwd(do.to(cuda), w.to(cuda), f.to(cuda), idx.to(cuda))
+    rdw, rdf = oracle.weighted_features_bwd(do, w, f, idx)
+    assert rel_err(dw.cpu(), rdw) < tol
+    assert rel_err(df.cpu(), rdf) < (TOL_BWD if dtype == torch.float32 else tol)
+
+
+def test_baseline_config1_chain(cuda):
+    """Config 1: KNN(K=48) -> 4-head neighbourhood attention -> weighted gather to M=1024 (fp32)."""
+    from affmae_b200.kernels.knn import knn
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd
+    from affmae_b200.kernels.weighted_gather import weighted_gather
+    gen = torch.Generator().manual_seed(0)
+    B, N, C, K, H = 2, 4096, 128, 48, 4
+    pos = torch.rand((B, N, 2), generator=gen) * 64
+    x = torch.randn((B, N, C), generator=gen)
+    w = torch.softmax(torch.randn((B, 1024, K), generator=gen), -1)
+    idx = knn(pos.to(cuda), pos.to(cuda), K)
+    ridx = oracle.knn(pos, pos, K)
+    assert torch.equal(idx.cpu(), ridx)
+    xh = x.view(B, N, H, C // H).permute(0, 2, 1, 3).contiguous()
+    o, _ = launch_flash_nbhood_attn_fwd(xh.to(cuda), xh.to(cuda), xh.to(cuda), idx, (C // H) ** -0.5)
+    ro, _ = oracle.nbhd_attn_fwd(xh, xh, xh, ridx, (C // H) ** -0.5)
+    assert rel_err(o.cpu(), ro) < TOL_F32
+    y = o.permute(0, 2, 1, 3).reshape(B, N, C)
+    out = weighted_gather(idx[:, :1024], w.to(cuda), y)
+    rout = oracle.weighted_features_fwd(w[..., None], ro.permute(0, 2, 1, 3).reshape(B, N, C), ridx[:, :1024])[:, :, 0]
+    assert rel_err(out.cpu(), rout) < TOL_F32
+
+
+# ------------------------------------------------------ deformable attention
+@pytest.mark.parametrize("tag", ["cross", "cross_grid"])
+def test_deform_cross_golden(cuda, tag):
+    from affmae_b200.kernels.fused_deform_attn import (fused_knn_deform_cross_attn_forward_save,
+                                                       fused_knn_deform_cross_attn_backward)
+    g = golden(f"deform_{tag}")
+    G = _to(g, cuda)
+    out, ki, kd = fused_knn_deform_cross_attn_forward_save(G["qpos"], G["kvpos"], G["off"], G["aw"], G["val"],
+                                                           G["power"])
+    assert torch.equal(ki.cpu(), g["knn_idx"])
+    assert torch.equal(kd.cpu(), g["knn_d2"])
+    assert rel_err(out.cpu(), g["out"]) < TOL_F32
+    grads = fused_knn_deform_cross_attn_backward(G["dout"], G["qpos"], G["kvpos"], G["off"], G["aw"], G["val"],
+                                                 G["power"], ki, kd)
+    for name, a in zip(["d_qpos", "d_kvpos", "d_off", "d_aw", "d_val", "d_power"], grads):
+        assert rel_err(a.cpu(), g[name]) < TOL_BWD, name
+
+
+def test_deform_self_golden(cuda):
+    from affmae_b200.kernels.fused_deform_attn import FusedKNNDeformSelfAttnFunction
+    g = golden("deform_self")
+    G = _to(g, cuda)
+    leaves = [G[n].clone().requires_grad_() for n in ("pos", "off", "aw", "val", "power")]
+    out = FusedKNNDeformSelfAttnFunction.apply(*leaves, 2)
+    assert rel_err(out.detach().cpu(), g["out"]) < TOL_F32
+    out.backward(G["dout"])
+    for name, t in zip(["d_pos", "d_off", "d_aw", "d_val", "d_power"], leaves):
+        assert rel_err(t.grad.cpu(), g[name].reshape(t.shape)) < TOL_BWD, name
+
+
+def _deform_inputs(B, Nq, kv_side, H, C, dtype, seed, integer=False):
+    gen = torch.Generator().manual_seed(seed)
+    ys, xs = torch.meshgrid(torch.arange(float(kv_side)), torch.arange(float(kv_side)), indexing="ij")
+    kv = torch.stack([xs, ys], -1).reshape(1, -1, 2).expand(B, -1, -1).clone()
+    if not integer:
+        kv = kv + (torch.rand(kv.shape, generator=gen) - 0.5) * 0.8
+    qp = torch.rand((B, Nq, 2), generator=gen) * kv_side
+    off = torch.randn((B, Nq, H, 4, 2), generator=gen) * 2
+    if integer:
+        qp = qp.floor()
+        off = off.round()
+    aw = torch.softmax(torch.randn((B, Nq, H, 4), generator=gen), -1)
+    val = torch.randn((B, kv.shape[1], H, C), generator=gen).to(dtype)
+    do = torch.randn((B, Nq, H, C), generator=gen).to(dtype)
+    return qp, kv, off, aw, val, torch.tensor(1.7), do
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_LP)])
+@pytest.mark.parametrize("integer", [False, True])
+@pytest.mark.parametrize("H,C", [(8, 32), (6, 64), (3, 16)])
+def test_deform_cross_random(cuda, dtype, tol, integer, H, C):
+    from affmae_b200.kernels.fused_deform_attn import (fused_knn_deform_cross_attn_forward_save,
+                                                       fused_knn_deform_cross_attn_backward)
+    qp, kv, off, aw, val, power, do = _deform_inputs(2, 300, 40, H, C, dtype, seed=H * C, integer=integer)
+    args = [t.to(cuda) for t in (qp, kv, off, aw, val, power)]
+    out, ki, kd = fused_knn_deform_cross_attn_forward_save(*args)
+    rout, ridx, rd2 = oracle.deform_knn_fwd(qp, kv, off, aw, val, power)
+    assert torch.equal(ki.cpu().long(), ridx)
+    assert torch.equal(kd.cpu(), rd2)
+    assert rel_err(out.cpu(), rout) < tol
+    grads = fused_knn_deform_cross_attn_backward(do.to(cuda), *args, ki, kd)
+    rgrads = oracle.deform_knn_bwd(do, qp, kv, off, aw, val, power, ridx, rd2)
+    btol = TOL_BWD if dtype == torch.float32 else tol
+    for name, a, b in zip(["d_qpos", "d_kvpos", "d_off", "d_aw", "d_val", "d_power"], grads, rgrads):
+        assert rel_err(a.cpu(), b) < btol, name
+
+
+def test_deform_far_samples_and_duplicates(cuda):
+    """Samples far outside the kv bounding box and duplicated kv positions."""
+    from affmae_b200.kernels.fused_deform_attn import fused_knn_deform_cross_attn_forward_save
+    qp, kv, off, aw, val, power, _ = _deform_inputs(1, 64, 10, 2, 8, torch.float32, seed=5)
+    off = off * 40
+    kv[:, 50:60] = kv[:, 10:20]
+    out, ki, kd = fused_knn_deform_cross_attn_forward_save(*[t.to(cuda) for t in (qp, kv, off, aw, val, power)])
+    rout, ridx, rd2 = oracle.deform_knn_fwd(qp, kv, off, aw, val, power)
+    assert torch.equal(ki.cpu().long(), ridx)
+    assert rel_err(out.cpu(), rout) < TOL_F32
+
+
+def test_deform_nbidx_golden(cuda):
+    from affmae_b200.kernels.fused_deform_attn import FusedDeformAttnFunction
+    g = golden("deform_nbidx")
+    G = _to(g, cuda)
+    leaves = {n: G[n].clone().requires_grad_() for n in ("sl", "kvpos", "power", "aw", "val")}
+    out = FusedDeformAttnFunction.apply(leaves["sl"], leaves["kvpos"], G["nb"], leaves["power"], leaves["aw"],
+                                        leaves["val"], 2, None)
+    assert rel_err(out.detach().cpu(), g["out"]) < TOL_F32
+    out.backward(G["dout"])
+    for name, key in [("d_sl", "sl"), ("d_kvpos", "kvpos"), ("d_power", "power"), ("d_aw", "aw"), ("d_val", "val")]:
+        assert rel_err(leaves[key].grad.cpu(), g[name]) < TOL_BWD, name
+
+
+def test_mssample_golden(cuda):
+    from affmae_b200.kernels.mssample import MSSampleFunction
+    g = golden("mssample")
+    G = _to(g, cuda)
+    sl = G["sl"].clone().requires_grad_()
+    kv = G["kvpos"].clone().requires_grad_()
+    p = G["power"].clone().requires_grad_()
+    w = MSSampleFunction.apply(sl, kv, G["nb"], p, 2)
+    assert rel_err(w.detach().cpu(), g["w"]) < TOL_F32
+    w.backward(G["dw"])
+    assert rel_err(sl.grad.cpu(), g["d_sl"]) < TOL_BWD
+    assert rel_err(kv.grad.cpu(), g["d_kvpos"]) < TOL_BWD
+    assert rel_err(p.grad.cpu(), g["d_power"]) < TOL_BWD
+
+
+def test_msdetrpc_golden(cuda):
+    from affmae_b200.kernels.msdetrpc import MSDETRPCFunction
+    g = golden("msdetrpc")
+    G = _to(g, cuda)
+    leaves = {n: G[n].clone().requires_grad_() for n in ("w", "attn", "val")}
+    out = MSDETRPCFunction.apply(G["idx"], leaves["w"], leaves["attn"], leaves["val"])
+    assert rel_err(out.detach().cpu(), g["out"]) < TOL_F32
+    out.backward(G["dout"])
+    for name, key in [("d_w", "w"), ("d_attn", "attn"), ("d_val", "val")]:
+        assert rel_err(leaves[key].grad.cpu(), g[name]) < TOL_BWD, name
+
+
+def test_pos_bias_gather(cuda):
+    from affmae_b200.kernels.pos_bias import pos_bias_gather
+    gen = torch.Generator().manual_seed(11)
+    T, H, B, N, M = 255 * 255, 4, 2, 300, 48
+    table = torch.randn((T, H), generator=gen)
+    pe = torch.randint(0, T, (B, N, M), generator=gen)
+    t = table.to(cuda).requires_grad_()
+    out = pos_bias_gather(t, pe.to(cuda))
+    assert torch.equal(out.detach().cpu(), oracle.pos_bias_fwd(table, pe).float())
+    g = torch.randn((B, H, N, M), generator=gen)
+    out.backward(g.to(cuda))
+    assert rel_err(t.grad.cpu(), oracle.pos_bias_bwd(g, pe, T)) < TOL_BWD

@@ -43,7 +43,10 @@ wf_fwd_kernel(const T* __restrict__ w, const T* __restrict__ feat, const int32_t
   const int32_t* ir = idx + r * M;
   const T* wr = w + r * (int64_t)M * IC;
   const T* fb = feat + b * N * C;
-  for (int c0 = lane * EPL; c0 < C; c0 += 32 * EPL) {
+  // the channel loop is warp-uniform (shuffles inside); lanes past C idle
+  for (int cb = 0; cb < C; cb += 32 * EPL) {
+    const int c0 = cb + lane * EPL;
+    const bool act = c0 < C;
     float acc[ICT][EPL];
 #pragma unroll
     for (int i = 0; i < ICT; ++i)
@@ -67,6 +70,7 @@ wf_fwd_kernel(const T* __restrict__ w, const T* __restrict__ feat, const int32_t
         float wv[ICT];
 #pragma unroll
         for (int i = 0; i < ICT; ++i) wv[i] = __shfl_sync(0xffffffffu, my_w[i], t);
+        if (!act) continue;
         float f[EPL];
         ld_chunk<T, EPL>(fb + (int64_t)id * C + c0, f, C - c0);
 #pragma unroll
@@ -75,6 +79,7 @@ wf_fwd_kernel(const T* __restrict__ w, const T* __restrict__ feat, const int32_t
           for (int e = 0; e < EPL; ++e) acc[i][e] = fmaf(wv[i], f[e], acc[i][e]);
       }
     }
+    if (!act) continue;
 #pragma unroll
     for (int i = 0; i < ICT; ++i) {
       if (ic0 + i >= IC) break;

@@ -363,3 +363,50 @@ def test_pos_bias_gather(cuda):
     g = torch.randn((B, H, N, M), generator=gen)
     out.backward(g.to(cuda))
     assert rel_err(t.grad.cpu(), oracle.pos_bias_bwd(g, pe, T)) < TOL_BWD
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mask_heads", [0, 1, 4])
+def test_local_attn_clustered_tensor_core_path(cuda, dtype, mask_heads):
+    """Cluster-structured neighbourhoods (the model's and config 3's) take the
+    tensor-core path; random neighbourhoods above take the CUDA-core fallback."""
+    from affmae_b200.workloads import nbhd_attention_inputs
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    inp = nbhd_attention_inputs(B=2, side=48, H=4, dtype=dtype, seed=mask_heads, device=cuda)
+    B, H, N, D = inp["q"].shape
+    M = inp["member_idx"].shape[-1]
+    mask = None
+    if mask_heads:
+        gen = torch.Generator().manual_seed(9)
+        mask = (torch.rand((B, mask_heads, N, M), generator=gen) > 0.15).to(cuda)
+        mask[0, 0, 5] = False  # a fully masked row (blank token keeps it finite)
+    kw = dict(bias=inp["bias"], mask=mask, blank_k=inp["blank_k"], blank_v=inp["blank_v"])
+    o, lse = launch_flash_nbhood_attn_fwd(inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["scale"], **kw)
+    cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in kw.items()}
+    ro, rlse = oracle.nbhd_attn_fwd(inp["q"].cpu(), inp["k"].cpu(), inp["v"].cpu(), inp["member_idx"].cpu(),
+                                    inp["scale"], **cpu)
+    assert rel_err(o.cpu(), ro) < TOL_LP
+    assert rel_err(lse.cpu(), rlse) < 1e-3
+    grads = launch_flash_nbhood_attn_bwd(inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["scale"], o, lse,
+                                         inp["dout"], **kw)
+    ref = oracle.nbhd_attn_bwd(inp["q"].cpu(), inp["k"].cpu(), inp["v"].cpu(), inp["member_idx"].cpu(),
+                               inp["scale"], o.cpu(), lse.cpu(), inp["dout"].cpu(), **cpu)
+    for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
+        assert rel_err(a.cpu(), b) < TOL_LP, name
+
+
+def test_local_attn_duplicate_neighbours_tensor_core(cuda):
+    """Repeated indices inside one neighbour list (allowed by the API) on the tensor-core path."""
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    inp = _attn_inputs(1, 2, 48, 32, 16, torch.bfloat16, seed=5)
+    inp["mi"] = torch.randint(0, 10, inp["mi"].shape, dtype=torch.int32)  # few keys => many duplicates
+    G = _to(inp, cuda)
+    kw = lambda d: dict(bias=d["bias"], mask=d["mask"], blank_k=d["blank_k"], blank_v=d["blank_v"])
+    o, lse = launch_flash_nbhood_attn_fwd(G["q"], G["k"], G["v"], G["mi"], 32 ** -0.5, **kw(G))
+    ro, _ = oracle.nbhd_attn_fwd(inp["q"], inp["k"], inp["v"], inp["mi"], 32 ** -0.5, **kw(inp))
+    assert rel_err(o.cpu(), ro) < TOL_LP
+    grads = launch_flash_nbhood_attn_bwd(G["q"], G["k"], G["v"], G["mi"], 32 ** -0.5, o, lse, G["do"], **kw(G))
+    ref = oracle.nbhd_attn_bwd(inp["q"], inp["k"], inp["v"], inp["mi"], 32 ** -0.5, o.cpu(), lse.cpu(), inp["do"],
+                               **kw(inp))
+    for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
+        assert rel_err(a.cpu(), b) < TOL_LP, name

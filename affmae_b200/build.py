@@ -51,7 +51,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     OBJ_DIR.mkdir(parents=True, exist_ok=True)
     cc = nvcc()
     hdrs = sorted(list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h")))
-    flags = NVCC_FLAGS + list(extra_flags or [])
+    flags = NVCC_FLAGS + list(extra_flags or []) + os.environ.get("AFFB_NVCC_EXTRA", "").split()
     jobs, objs = [], []
     for src in sorted(CSRC.glob("*.cu")):
         obj = OBJ_DIR / (src.stem + ".o")

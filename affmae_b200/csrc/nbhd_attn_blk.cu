@@ -1,0 +1,476 @@
+// Neighbourhood attention on the tensor cores for cluster-block neighbour
+// lists (bf16 / fp16, head_dim 32).
+//
+// In AFFMAE the neighbour list of a token is the concatenation of the 8
+// members of its nearest clusters, and tokens are ordered so that cluster c
+// is tokens [8c, 8c+8) (BasicLayer.forward, src/layers/aff.py:445-453;
+// space_filling_cluster, src/utils/geometry.py:314-317).  Each list is then
+// M/8 runs idx[8j .. 8j+7] = 8c_j + (0..7).  This kernel exploits that:
+//   * per tile of 16 queries the union is a set of clusters (<= UCAP/8),
+//     found by hashing the M/8 cluster ids of each row (not M keys);
+//   * one mma n-tile (8 columns) is exactly one cluster, so the attended
+//     pattern is a [16 x clusters] table of list positions j (or absent),
+//     shared by all heads; bias[q, 8j + r] is read straight from the staged
+//     bias rows (no per-head scatter), and dbias is stored straight from the
+//     accumulator fragments;
+//   * K/V rows of a cluster are 512 contiguous bytes per head.
+// Semantics are those of the CUDA-core path (nbhd_row.cuh; reference
+// local_attn.py:224-553).  A tile that is not of this form (or whose cluster
+// union exceeds UCAP/8, or that lists a cluster twice) is appended to a list
+// processed afterwards by the neighbour-union kernels (nbhd_attn_tc.cu).
+//
+// Per warp and head the work is a flash-attention loop over 16-key chunks
+// (two clusters): S = Q K^T on mma.sync in registers, online softmax in the
+// accumulator layout, O += P V.  The backward recomputes S and dP = dO V^T,
+// keeps dQ in registers, and scatters dK = dS^T Q, dV = P^T dO per chunk.
+#include "nbhd_tc.cuh"
+#include "nbhd_mma.cuh"
+
+namespace affb {
+
+constexpr int UCLU = UCAP / 8;   // clusters per tile on this path
+constexpr int CHS = 256;         // cluster hash slots
+constexpr int BPT = 24;          // 16-bit row stride of the per-warp 16x16 P / dS tiles
+
+struct BlkSetup {
+  alignas(16) int idx[TQ * MMAX];  // staged neighbour rows
+  int ukey[UCAP];                  // key rows of the cluster union (8 per cluster)
+  int jtab[TQ][UCLU];              // list position j of cluster slot u in row q, -1 absent
+  int hkey[CHS], hval[CHS];
+  int warp_tot[NW];
+  int nclu, fail;
+};
+
+template <typename T>
+struct BlkWarpFwd {
+  alignas(16) T Q[TQ * KST];
+  alignas(16) T bias[TQ * MMAX];
+  alignas(16) T KV[2][2][16 * KST];
+};
+template <typename T>
+struct BlkWarpBwd {
+  alignas(16) T Q[TQ * KST];
+  alignas(16) T dO[TQ * KST];
+  alignas(16) T bias[TQ * MMAX];
+  alignas(16) T KV[2][2][16 * KST];
+  alignas(16) T P[TQ * BPT];
+  alignas(16) T dS[TQ * BPT];
+};
+template <typename T>
+struct BlkFwdSmem {
+  BlkSetup setup;
+  BlkWarpFwd<T> w[NW];
+};
+template <typename T>
+struct BlkBwdSmem {
+  BlkSetup setup;
+  BlkWarpBwd<T> w[NW];
+};
+
+__device__ __forceinline__ uint32_t clu_slot(int key) { return ((uint32_t)key * 2654435761u) >> 24; }
+
+// Checks the cluster-block form of the tile and builds its cluster union.
+// Returns the number of clusters, or -1 when the tile needs the general path.
+__device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, int n0, int nq, int N, int M) {
+  const int t = threadIdx.x;
+  const int J = M >> 3;  // clusters per list
+  {
+    const int32_t* src = midx + ((int64_t)b * N + n0) * M;
+    const int nch = TQ * M / 4;  // 16-byte chunks of int32
+    for (int i = t; i < nch; i += TC_THREADS) {
+      const bool ok = (i * 4) / M < nq;
+      cp_async16(s.idx + i * 4, src + (ok ? i * 4 : 0), ok);
+    }
+    cp_commit();
+  }
+  for (int i = t; i < CHS; i += TC_THREADS) s.hkey[i] = -1;
+  for (int i = t; i < TQ * UCLU; i += TC_THREADS) (&s.jtab[0][0])[i] = -1;
+  if (t == 0) s.fail = 0;
+  cp_wait<0>();
+  __syncthreads();
+  // item (q, j) per thread: verify the run, insert its cluster id
+  int cid = -1;
+  const int q = t / 8, j = t % 8;  // TQ * 8 = 128 items cover J <= 8
+  if (q < nq && j < J) {
+    const int* run = s.idx + q * M + 8 * j;
+    const int c0 = run[0];
+    bool ok = c0 >= 0 && (c0 & 7) == 0 && c0 + 8 <= N;
+#pragma unroll
+    for (int r = 1; r < 8; ++r) ok = ok && run[r] == c0 + r;
+    if (ok) {
+      cid = c0 >> 3;
+      uint32_t h = clu_slot(cid);
+      while (true) {
+        const int old = atomicCAS(&s.hkey[h], -1, cid);
+        if (old == -1 || old == cid) break;
+        h = (h + 1) & (CHS - 1);
+      }
+    } else {
+      s.fail = 1;
+    }
+  }
+  __syncthreads();
+  if (s.fail) return -1;
+  // compact occupied slots (2 per thread) with a block scan
+  const int lane = t & 31, w = t >> 5;
+  const int c = (s.hkey[2 * t] >= 0) + (s.hkey[2 * t + 1] >= 0);
+  int x = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s.warp_tot[w] = x;
+  __syncthreads();
+  int base = 0, total = 0;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    if (i < w) base += s.warp_tot[i];
+    total += s.warp_tot[i];
+  }
+  if (total > UCLU) return -1;
+  int pos = base + x - c;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int key = s.hkey[2 * t + i];
+    if (key >= 0) {
+      s.hval[2 * t + i] = pos;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) s.ukey[pos * 8 + r] = key * 8 + r;
+      ++pos;
+    }
+  }
+  __syncthreads();
+  if (cid >= 0) {
+    uint32_t h = clu_slot(cid);
+    while (s.hkey[h] != cid) h = (h + 1) & (CHS - 1);
+    if (atomicExch(&s.jtab[q][s.hval[h]], j) != -1) s.fail = 1;  // cluster listed twice in a row
+  }
+  __syncthreads();
+  return s.fail ? -1 : total;
+}
+
+__device__ __forceinline__ void push_fallback(const NbhdArgs& a, int tile) {
+  if (threadIdx.x == 0) a.fb_list[atomicAdd(a.fb_count, 1)] = tile;
+}
+
+// Bias pair (columns 8j + 2tq, +1) of row `row` from the staged rows, masked
+// entries (mask == 0) and absent clusters giving -inf.
+template <typename T>
+__device__ __forceinline__ void bias_pair(const NbhdArgs& a, const T* sbias, const uint8_t* mrow, int M, int row,
+                                          int jv, int tq, float& b0, float& b1) {
+  if (jv < 0) { b0 = b1 = -INFINITY; return; }
+  const int col = 8 * jv + 2 * tq;
+  if (a.bias) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(sbias + row * M + col);
+    const T* hp = reinterpret_cast<const T*>(&u);
+    b0 = io<T>::ld(hp);
+    b1 = io<T>::ld(hp + 1);
+  } else {
+    b0 = b1 = 0.f;
+  }
+  if (mrow) {
+    if (mrow[row * M + col] == 0) b0 = -INFINITY;
+    if (mrow[row * M + col + 1] == 0) b1 = -INFINITY;
+  }
+}
+
+template <typename T>
+__device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>& w, int b, int h, int n0,
+                             int nq, int nclu) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int N = a.N, M = a.M;
+  const int U = nclu * 8, nchunk = (nclu + 1) / 2;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const T* kb = (const T*)a.k + bh * N * TD;
+  const T* vb = (const T*)a.v + bh * N * TD;
+  const int* ukey = s.ukey;
+  auto rows_u = [&](int u0) { return [=](int i) -> int64_t { return u0 + i < U ? ukey[u0 + i] : -1; }; };
+  warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, [=](int i) -> int64_t { return i < nq ? i : -1; });
+  if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
+  cp_commit();
+  warp_load16(w.KV[0][0], kb, rows_u(0));
+  warp_load16(w.KV[0][1], vb, rows_u(0));
+  cp_commit();
+  const uint8_t* mrow = a.mask ? a.mask + (((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N + n0) * M : nullptr;
+  int ex[2] = {0, 0};
+  if (mrow) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = g + hf * 8;
+      int cnt = 0;
+      if (row < nq)
+        for (int e = tq; e < M; e += 4) cnt += mrow[row * M + e] == 0;
+#pragma unroll
+      for (int o = 1; o < 4; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+      ex[hf] = cnt;
+    }
+  }
+  cp_wait<1>();
+  __syncwarp();
+  uint32_t aq[2][4];
+  load_a_frags(aq, w.Q);
+  float sbv[2] = {-INFINITY, -INFINITY};
+  if (a.blank_k) {
+    rows_dot(w.Q, (const T*)a.blank_k + (int64_t)h * TD, sbv[0], sbv[1]);
+    sbv[0] *= a.scale;
+    sbv[1] *= a.scale;
+  }
+  float m[2] = {-1e11f, -1e11f}, l[2] = {0.f, 0.f};
+  float o[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int c = 0; c < nchunk; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunk) {
+      warp_load16(w.KV[buf ^ 1][0], kb, rows_u((c + 1) * 16));
+      warp_load16(w.KV[buf ^ 1][1], vb, rows_u((c + 1) * 16));
+    }
+    cp_commit();
+    cp_wait<1>();
+    __syncwarp();
+    float x[2][4];
+    mma_chunk_nt<T>(x, aq, w.KV[buf][0], 0);
+    float cm[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = g + hf * 8;
+        float b0, b1;
+        bias_pair<T>(a, w.bias, mrow, M, row, s.jtab[row][2 * c + nt], tq, b0, b1);
+        x[nt][2 * hf] = x[nt][2 * hf] * a.scale + b0;
+        x[nt][2 * hf + 1] = x[nt][2 * hf + 1] * a.scale + b1;
+        cm[hf] = fmaxf(cm[hf], fmaxf(x[nt][2 * hf], x[nt][2 * hf + 1]));
+      }
+    }
+    float al[2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      cm[hf] = fmaxf(cm[hf], __shfl_xor_sync(0xffffffffu, cm[hf], 1));
+      cm[hf] = fmaxf(cm[hf], __shfl_xor_sync(0xffffffffu, cm[hf], 2));
+      const float nm = fmaxf(m[hf], cm[hf]);
+      al[hf] = __expf(m[hf] - nm);
+      m[hf] = nm;
+      l[hf] *= al[hf];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { o[i][0] *= al[0]; o[i][1] *= al[0]; o[i][2] *= al[1]; o[i][3] *= al[1]; }
+    float p[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        p[nt][e] = __expf(x[nt][e] - m[e >> 1]);
+        l[e >> 1] += p[nt][e];
+      }
+    const uint32_t pa[4] = {pack2<T>(p[0][0], p[0][1]), pack2<T>(p[0][2], p[0][3]),
+                            pack2<T>(p[1][0], p[1][1]), pack2<T>(p[1][2], p[1][3])};
+    mma_chunk_pv<T>(o, pa, w.KV[buf][1], 0);
+    __syncwarp();
+  }
+  const int pad = padded_neighbours(M) - M;
+  const T* bvp = a.blank_v ? (const T*)a.blank_v + (int64_t)h * TD : nullptr;
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    float lf = l[hf];
+    lf += __shfl_xor_sync(0xffffffffu, lf, 1);
+    lf += __shfl_xor_sync(0xffffffffu, lf, 2);
+    const float mm = a.blank_k ? fmaxf(m[hf], sbv[hf]) : m[hf];
+    const float alf = expf(m[hf] - mm);
+    const float pb = a.blank_k ? expf(sbv[hf] - mm) : 0.f;
+    lf = lf * alf + pb + (float)(ex[hf] + pad) * expf(-1e11f - mm);
+    const int row = g + hf * 8;
+    if (row >= nq) continue;
+    const float lse = mm + logf(lf + 1e-12f);
+    const float inv = expf(mm - lse);
+    T* orow = (T*)a.out + (bh * N + n0 + row) * TD;
+#pragma unroll
+    for (int dt = 0; dt < 4; ++dt) {
+      const int col = dt * 8 + 2 * tq;
+      float v0 = o[dt][2 * hf] * alf, v1 = o[dt][2 * hf + 1] * alf;
+      if (bvp) { v0 += pb * ldf(bvp + col); v1 += pb * ldf(bvp + col + 1); }
+      *reinterpret_cast<uint32_t*>(orow + col) = pack2<T>(v0 * inv, v1 * inv);
+    }
+    if (tq == 0) a.lse[bh * N + n0 + row] = lse;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS) nbhd_blk_fwd_kernel(NbhdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BlkFwdSmem<T>& s = *reinterpret_cast<BlkFwdSmem<T>*>(smem_raw);
+  const int N = a.N;
+  const int tiles = (N + TQ - 1) / TQ;
+  const int b = blockIdx.x / tiles;
+  const int n0 = (blockIdx.x % tiles) * TQ;
+  const int nq = min(TQ, N - n0);
+  const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
+  if (nclu < 0) { push_fallback(a, blockIdx.x); return; }
+  const int warp = threadIdx.x >> 5;
+  for (int h = warp; h < a.H; h += NW) blk_fwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+}
+
+template <typename T>
+__device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>& w, int b, int h, int n0,
+                             int nq, int nclu) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int N = a.N, M = a.M;
+  const int U = nclu * 8, nchunk = (nclu + 1) / 2;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const T* kb = (const T*)a.k + bh * N * TD;
+  const T* vb = (const T*)a.v + bh * N * TD;
+  const int* ukey = s.ukey;
+  auto rows_u = [&](int u0) { return [=](int i) -> int64_t { return u0 + i < U ? ukey[u0 + i] : -1; }; };
+  auto rows_q = [=](int i) -> int64_t { return i < nq ? i : -1; };
+  warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, rows_q);
+  warp_load16(w.dO, (const T*)a.dout + (bh * N + n0) * TD, rows_q);
+  if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
+  cp_commit();
+  warp_load16(w.KV[0][0], kb, rows_u(0));
+  warp_load16(w.KV[0][1], vb, rows_u(0));
+  cp_commit();
+  const uint8_t* mrow = a.mask ? a.mask + (((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N + n0) * M : nullptr;
+  float dl[2], ls[2];
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int row = g + hf * 8;
+    float p = 0.f;
+    ls[hf] = 0.f;
+    if (row < nq) {
+      float ov[8], dv[8];
+      ld8((const T*)a.o + (bh * N + n0 + row) * TD + tq * 8, ov);
+      ld8((const T*)a.dout + (bh * N + n0 + row) * TD + tq * 8, dv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) p = fmaf(ov[e], dv[e], p);
+      ls[hf] = a.lse[bh * N + n0 + row];
+    }
+    p += __shfl_xor_sync(0xffffffffu, p, 1);
+    p += __shfl_xor_sync(0xffffffffu, p, 2);
+    dl[hf] = p;
+  }
+  cp_wait<1>();
+  __syncwarp();
+  uint32_t aq[2][4], ado[2][4];
+  load_a_frags(aq, w.Q);
+  load_a_frags(ado, w.dO);
+  float dsb[2] = {0.f, 0.f};
+  if (a.blank_k) {
+    float sb[2], dpb[2], pbv[2];
+    rows_dot(w.Q, (const T*)a.blank_k + (int64_t)h * TD, sb[0], sb[1]);
+    rows_dot(w.dO, (const T*)a.blank_v + (int64_t)h * TD, dpb[0], dpb[1]);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      pbv[hf] = (g + hf * 8) < nq ? expf(sb[hf] * a.scale - ls[hf]) : 0.f;
+      dsb[hf] = pbv[hf] * (dpb[hf] - dl[hf]);
+    }
+    float gk = 0.f, gv = 0.f;
+#pragma unroll
+    for (int row = 0; row < TQ; ++row) {
+      const int src = (row & 7) * 4;
+      const float ds_r = __shfl_sync(0xffffffffu, row < 8 ? dsb[0] : dsb[1], src);
+      const float pb_r = __shfl_sync(0xffffffffu, row < 8 ? pbv[0] : pbv[1], src);
+      gk = fmaf(ds_r, io<T>::ld(w.Q + row * KST + lane), gk);
+      gv = fmaf(pb_r, io<T>::ld(w.dO + row * KST + lane), gv);
+    }
+    red_add(a.dbk + (int64_t)h * TD + lane, gk * a.scale);
+    red_add(a.dbv + (int64_t)h * TD + lane, gv);
+  }
+  T* dbase = a.dbias ? (T*)a.dbias + (bh * N + n0) * M : nullptr;
+  float qacc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
+  for (int c = 0; c < nchunk; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunk) {
+      warp_load16(w.KV[buf ^ 1][0], kb, rows_u((c + 1) * 16));
+      warp_load16(w.KV[buf ^ 1][1], vb, rows_u((c + 1) * 16));
+    }
+    cp_commit();
+    cp_wait<1>();
+    __syncwarp();
+    float sx[2][4], dp[2][4];
+    mma_chunk_nt<T>(sx, aq, w.KV[buf][0], 0);
+    mma_chunk_nt<T>(dp, ado, w.KV[buf][1], 0);
+    float p[2][4], ds[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int lc = nt * 8 + 2 * tq;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = g + hf * 8;
+        const int jv = s.jtab[row][2 * c + nt];
+        float b0, b1;
+        bias_pair<T>(a, w.bias, mrow, M, row, jv, tq, b0, b1);
+        p[nt][2 * hf] = __expf(sx[nt][2 * hf] * a.scale + b0 - ls[hf]);
+        p[nt][2 * hf + 1] = __expf(sx[nt][2 * hf + 1] * a.scale + b1 - ls[hf]);
+        ds[nt][2 * hf] = p[nt][2 * hf] * (dp[nt][2 * hf] - dl[hf]);
+        ds[nt][2 * hf + 1] = p[nt][2 * hf + 1] * (dp[nt][2 * hf + 1] - dl[hf]);
+        const uint32_t dpk = pack2<T>(ds[nt][2 * hf], ds[nt][2 * hf + 1]);
+        if (dbase && jv >= 0 && row < nq)
+          *reinterpret_cast<uint32_t*>(dbase + row * M + 8 * jv + 2 * tq) = dpk;
+        *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
+        *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);
+      }
+    }
+    const uint32_t da[4] = {pack2<T>(ds[0][0], ds[0][1]), pack2<T>(ds[0][2], ds[0][3]),
+                            pack2<T>(ds[1][0], ds[1][1]), pack2<T>(ds[1][2], ds[1][3])};
+    mma_chunk_pv<T>(qacc, da, w.KV[buf][0], 0);
+    __syncwarp();
+    mma_chunk_scatter<T>(w.dS, BPT, w.Q, ukey, U, c * 16, a.scale, a.dk + bh * N * TD);
+    mma_chunk_scatter<T>(w.P, BPT, w.dO, ukey, U, c * 16, 1.f, a.dv + bh * N * TD);
+    __syncwarp();
+  }
+  const T* bkp = a.blank_k ? (const T*)a.blank_k + (int64_t)h * TD : nullptr;
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int row = g + hf * 8;
+    if (row >= nq) continue;
+    T* qrow = (T*)a.dq + (bh * N + n0 + row) * TD;
+#pragma unroll
+    for (int dt = 0; dt < 4; ++dt) {
+      const int col = dt * 8 + 2 * tq;
+      float v0 = qacc[dt][2 * hf], v1 = qacc[dt][2 * hf + 1];
+      if (bkp) { v0 += dsb[hf] * ldf(bkp + col); v1 += dsb[hf] * ldf(bkp + col + 1); }
+      *reinterpret_cast<uint32_t*>(qrow + col) = pack2<T>(v0 * a.scale, v1 * a.scale);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS) nbhd_blk_bwd_kernel(NbhdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BlkBwdSmem<T>& s = *reinterpret_cast<BlkBwdSmem<T>*>(smem_raw);
+  const int N = a.N;
+  const int tiles = (N + TQ - 1) / TQ;
+  const int b = blockIdx.x / tiles;
+  const int n0 = (blockIdx.x % tiles) * TQ;
+  const int nq = min(TQ, N - n0);
+  const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
+  if (nclu < 0) { push_fallback(a, blockIdx.x); return; }
+  const int warp = threadIdx.x >> 5;
+  for (int h = warp; h < a.H; h += NW) blk_bwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+}
+
+template <typename K>
+static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStream_t st) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    set_error("nbhd_attn: cannot reserve %zu bytes of shared memory", smem);
+    return AFFB_ERR_CUDA;
+  }
+  const int64_t tiles = (int64_t)((a.N + TQ - 1) / TQ) * B;
+  kernel<<<(unsigned)tiles, TC_THREADS, smem, st>>>(a);
+  return AFFB_OK;
+}
+
+int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
+  if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_fwd_kernel<__nv_bfloat16>, sizeof(BlkFwdSmem<__nv_bfloat16>), a, B, st);
+  return launch_blk(nbhd_blk_fwd_kernel<__half>, sizeof(BlkFwdSmem<__half>), a, B, st);
+}
+
+int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
+  if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_bwd_kernel<__nv_bfloat16>, sizeof(BlkBwdSmem<__nv_bfloat16>), a, B, st);
+  return launch_blk(nbhd_blk_bwd_kernel<__half>, sizeof(BlkBwdSmem<__half>), a, B, st);
+}
+
+}  // namespace affb

@@ -250,6 +250,7 @@ def run_gpu(args, world, rank, local):
         dbv = torch.zeros(bv.shape, device=dev, dtype=torch.float32)
         kern_ms = []
         B, H, N, D = q.shape
+        ws = torch.empty(int(nat.lib().affb_nbhd_attn_workspace_bytes(B, N)), dtype=torch.uint8, device=dev)
         for _ in range(args.steps):
             flush.fill_(1)
             dk_acc.zero_(); dv_acc.zero_()
@@ -259,7 +260,8 @@ def run_gpu(args, world, rank, local):
             nat.call("affb_nbhd_attn_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
                      lse.data_ptr(), mi.data_ptr(), bias.data_ptr(), None, 1, bk.data_ptr(), bv.data_ptr(),
                      nat.BF16, B, H, N, D, CFG["nbhd"], float(scale), dq.data_ptr(), dk_acc.data_ptr(),
-                     dv_acc.data_ptr(), dbias.data_ptr(), dbk.data_ptr(), dbv.data_ptr(), stream.cuda_stream)
+                     dv_acc.data_ptr(), dbias.data_ptr(), dbk.data_ptr(), dbv.data_ptr(), ws.data_ptr(),
+                     stream.cuda_stream)
             c.record(stream)
             kern_ms.append((a, c))
         torch.cuda.synchronize()

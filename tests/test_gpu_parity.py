@@ -410,3 +410,25 @@ def test_local_attn_duplicate_neighbours_tensor_core(cuda):
                                **kw(inp))
     for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
         assert rel_err(a.cpu(), b) < TOL_LP, name
+
+
+def test_local_attn_mixed_block_and_general_tiles(cuda):
+    """Cluster-block tiles and general tiles in one call (block kernel + union kernel)."""
+    from affmae_b200.workloads import nbhd_attention_inputs
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    inp = nbhd_attention_inputs(B=2, side=40, H=4, dtype=torch.bfloat16, seed=3, device=cuda)
+    mi = inp["member_idx"].clone()
+    mi[0, 17, 5] = (mi[0, 17, 5] + 3) % mi.shape[1]          # breaks the run: general tile
+    mi[1, 100:116] = torch.flip(mi[1, 100:116], dims=[-1])    # reversed runs: general tiles
+    N = mi.shape[1]
+    mi[1, N - 3:] = torch.randint(0, N, (3, mi.shape[2]), dtype=torch.int32, device=cuda)
+    kw = dict(bias=inp["bias"], blank_k=inp["blank_k"], blank_v=inp["blank_v"])
+    o, lse = launch_flash_nbhood_attn_fwd(inp["q"], inp["k"], inp["v"], mi, inp["scale"], **kw)
+    cpu = {k: v.cpu() for k, v in kw.items()}
+    ro, _ = oracle.nbhd_attn_fwd(inp["q"].cpu(), inp["k"].cpu(), inp["v"].cpu(), mi.cpu(), inp["scale"], **cpu)
+    assert rel_err(o.cpu(), ro) < TOL_LP
+    grads = launch_flash_nbhood_attn_bwd(inp["q"], inp["k"], inp["v"], mi, inp["scale"], o, lse, inp["dout"], **kw)
+    ref = oracle.nbhd_attn_bwd(inp["q"].cpu(), inp["k"].cpu(), inp["v"].cpu(), mi.cpu(), inp["scale"], o.cpu(),
+                               lse.cpu(), inp["dout"].cpu(), **cpu)
+    for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
+        assert rel_err(a.cpu(), b) < TOL_LP, name

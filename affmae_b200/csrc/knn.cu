@@ -14,7 +14,9 @@
 // an insertion is a warp-wide shift by one slot done with two shuffles per
 // register.  Reference points are staged per block in shared memory in tiles;
 // every lane evaluates one reference point per step and a ballot selects the
-// few that beat the K-th distance, which are then inserted in index order.
+// few that beat the current K-th entry, which are then inserted.  The list is
+// ordered by (distance, index), which selects exactly the same K points in
+// the same order as the reference's ascending-index scan with strict '<'.
 #include "common.cuh"
 
 namespace affb {
@@ -38,7 +40,7 @@ template <typename T, int D, int KPL>
 __global__ void __launch_bounds__(KNN_WARPS * 32)
 knn_kernel(const T* __restrict__ query, const T* __restrict__ ref, int64_t M, int64_t N, int K,
            int64_t* __restrict__ out) {
-  __shared__ float sref[KNN_TILE * D];
+  __shared__ float sref[D][KNN_TILE];  // tile position r stored at slot (r % S) * 32 + r / S
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.y;
@@ -54,33 +56,47 @@ knn_kernel(const T* __restrict__ query, const T* __restrict__ ref, int64_t M, in
 #pragma unroll
   for (int j = 0; j < KPL; ++j) { ld[j] = 1e38f; li[j] = 0; }
   float kth = 1e38f;
+  int kth_i = 0;  // empty slots hold (1e38, 0), as in the reference's initial state
   const int kj = (K - 1) >> 5, kl = (K - 1) & 31;
 
   const T* rb = ref + b * N * D;
   for (int64_t t0 = 0; t0 < N; t0 += KNN_TILE) {
     const int tn = (N - t0) < KNN_TILE ? (int)(N - t0) : KNN_TILE;
+    const int S = (tn + 31) >> 5;
     __syncthreads();
-    for (int i = threadIdx.x; i < tn * D; i += blockDim.x) sref[i] = ldf(rb + t0 * D + i);
+    for (int i = threadIdx.x; i < tn; i += blockDim.x) {
+      const int slot = (i % S) * 32 + i / S;
+#pragma unroll
+      for (int d = 0; d < D; ++d) sref[d][slot] = ldf(rb + (t0 + i) * D + d);
+    }
     __syncthreads();
     if (!active) continue;
-    for (int base = 0; base < tn; base += 32) {
-      const int r = base + lane;
+    // Lane l scans tile positions l*S .. l*S + S - 1, so the 32 candidates of
+    // a step are spread over the tile; spatially ordered inputs then shrink
+    // the K-th distance quickly and few candidates are inserted.  Insertion
+    // compares (distance, index) lexicographically, so the scan order does
+    // not change the result.
+    for (int step = 0; step < S; ++step) {
+      const int r = lane * S + step;
       float dist = 0.f;
       bool cand = false;
       if (r < tn) {
-        dist = sqdist<D>(qp, sref + r * D);
-        cand = dist < kth;
+        float rp[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) rp[d] = sref[d][step * 32 + lane];
+        dist = sqdist<D>(qp, rp);
+        cand = dist < kth || (dist == kth && (int)(t0 + r) < kth_i);
       }
       unsigned bal = __ballot_sync(0xffffffffu, cand);
       while (bal) {
         const int src = __ffs(bal) - 1;
         bal &= bal - 1;
         const float cd = __shfl_sync(0xffffffffu, dist, src);
-        if (!(cd < kth)) continue;  // threshold moved since the ballot
-        const int ci = (int)(t0 + base + src);
+        const int ci = (int)t0 + src * S + step;
+        if (!(cd < kth || (cd == kth && ci < kth_i))) continue;  // threshold moved since the ballot
         int cnt = 0;
 #pragma unroll
-        for (int j = 0; j < KPL; ++j) cnt += (ld[j] <= cd);
+        for (int j = 0; j < KPL; ++j) cnt += (ld[j] < cd) || (ld[j] == cd && li[j] < ci);
         const int pos = __reduce_add_sync(0xffffffffu, cnt);
         float nd[KPL];
         int ni[KPL];
@@ -93,18 +109,20 @@ knn_kernel(const T* __restrict__ query, const T* __restrict__ ref, int64_t M, in
             const int wi = __shfl_sync(0xffffffffu, li[j - 1], 31);
             if (lane == 0) { up_d = wd; up_i = wi; }
           }
-          const int s = j * 32 + lane;
-          nd[j] = s < pos ? ld[j] : (s == pos ? cd : up_d);
-          ni[j] = s < pos ? li[j] : (s == pos ? ci : up_i);
+          const int s2 = j * 32 + lane;
+          nd[j] = s2 < pos ? ld[j] : (s2 == pos ? cd : up_d);
+          ni[j] = s2 < pos ? li[j] : (s2 == pos ? ci : up_i);
         }
         float kv = 0.f;
+        int ki = 0;
 #pragma unroll
         for (int j = 0; j < KPL; ++j) {
           ld[j] = nd[j];
           li[j] = ni[j];
-          if (j == kj) kv = nd[j];
+          if (j == kj) { kv = nd[j]; ki = ni[j]; }
         }
         kth = __shfl_sync(0xffffffffu, kv, kl);
+        kth_i = __shfl_sync(0xffffffffu, ki, kl);
       }
     }
   }

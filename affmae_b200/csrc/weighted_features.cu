@@ -171,19 +171,180 @@ wf_bwd_kernel(const T* __restrict__ dout, const T* __restrict__ w, const T* __re
   }
 }
 
+
+// Vectorised path (C % 8 == 0): lane = slot * GL + chunk, chunk covering 8
+// channels; the 32/GL lane groups work on different neighbours at once and
+// are summed at the end, so narrow rows (C = 96, 128) keep every lane busy.
+template <typename T, int ICT, int GL>
+__global__ void __launch_bounds__(WF_WARPS * 32)
+wf_fwd_grp_kernel(const T* __restrict__ w, const T* __restrict__ feat, const int32_t* __restrict__ idx,
+                  int64_t No, int M, int IC, int ic0, int64_t N, int C, T* __restrict__ out) {
+  constexpr int NS = 32 / GL;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * WF_WARPS + (threadIdx.x >> 5);
+  if (row >= No) return;
+  const int slot = lane / GL, ch = lane % GL;
+  const int64_t b = blockIdx.y;
+  const int64_t r = b * No + row;
+  const int32_t* ir = idx + r * M;
+  const T* wr = w + r * (int64_t)M * IC;
+  const T* fb = feat + b * N * C;
+  for (int cb = 0; cb < C; cb += GL * 8) {
+    const int c0 = cb + ch * 8;
+    const bool act = c0 < C;
+    float acc[ICT][8];
+#pragma unroll
+    for (int i = 0; i < ICT; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+    for (int m0 = 0; m0 < M; m0 += 32) {
+      const int m = m0 + lane;
+      int my_idx = 0;
+      float my_w[ICT];
+#pragma unroll
+      for (int i = 0; i < ICT; ++i) my_w[i] = 0.f;
+      if (m < M) {
+        my_idx = ir[m];
+#pragma unroll
+        for (int i = 0; i < ICT; ++i)
+          if (ic0 + i < IC) my_w[i] = ldf(wr + (int64_t)m * IC + ic0 + i);
+      }
+      const int cnt = min(32, M - m0);
+#pragma unroll 2
+      for (int t0 = 0; t0 < cnt; t0 += NS) {
+        const int t = t0 + slot;
+        const int id = __shfl_sync(0xffffffffu, my_idx, t & 31);
+        float wv[ICT];
+#pragma unroll
+        for (int i = 0; i < ICT; ++i) wv[i] = __shfl_sync(0xffffffffu, my_w[i], t & 31);
+        if (!act || t >= cnt) continue;
+        float f[8];
+        ld8(fb + (int64_t)id * C + c0, f);
+#pragma unroll
+        for (int i = 0; i < ICT; ++i)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(wv[i], f[e], acc[i][e]);
+      }
+    }
+#pragma unroll
+    for (int off = GL; off < 32; off <<= 1)
+#pragma unroll
+      for (int i = 0; i < ICT; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[i][e] += __shfl_xor_sync(0xffffffffu, acc[i][e], off);
+    if (!act || slot != 0) continue;
+#pragma unroll
+    for (int i = 0; i < ICT; ++i) {
+      if (ic0 + i >= IC) break;
+      st8(out + (r * IC + ic0 + i) * C + c0, acc[i]);
+    }
+  }
+}
+
+template <typename T, int ICT, int GL>
+__global__ void __launch_bounds__(WF_WARPS * 32)
+wf_bwd_grp_kernel(const T* __restrict__ dout, const T* __restrict__ w, const T* __restrict__ feat,
+                  const int32_t* __restrict__ idx, int64_t No, int M, int IC, int ic0, int64_t N, int C,
+                  T* __restrict__ dw, float* __restrict__ dfeat) {
+  constexpr int NS = 32 / GL;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * WF_WARPS + (threadIdx.x >> 5);
+  if (row >= No) return;
+  const int slot = lane / GL, ch = lane % GL;
+  const int64_t b = blockIdx.y;
+  const int64_t r = b * No + row;
+  const int32_t* ir = idx + r * M;
+  const T* wr = w + r * (int64_t)M * IC;
+  const T* dor = dout + r * (int64_t)IC * C;
+  const T* fb = feat + b * N * C;
+  float* dfb = dfeat + b * N * C;
+  for (int m0 = 0; m0 < M; m0 += 32) {
+    const int m = m0 + lane;
+    int my_idx = 0;
+    float my_w[ICT];
+#pragma unroll
+    for (int i = 0; i < ICT; ++i) my_w[i] = 0.f;
+    if (m < M) {
+      my_idx = ir[m];
+#pragma unroll
+      for (int i = 0; i < ICT; ++i)
+        if (ic0 + i < IC) my_w[i] = ldf(wr + (int64_t)m * IC + ic0 + i);
+    }
+    float my_dw[ICT];
+#pragma unroll
+    for (int i = 0; i < ICT; ++i) my_dw[i] = 0.f;
+    const int cnt = min(32, M - m0);
+    for (int t0 = 0; t0 < cnt; t0 += NS) {
+      const int t = t0 + slot;
+      const bool tv = t < cnt;
+      const int id = __shfl_sync(0xffffffffu, my_idx, t & 31);
+      float wv[ICT], part[ICT];
+#pragma unroll
+      for (int i = 0; i < ICT; ++i) { wv[i] = __shfl_sync(0xffffffffu, my_w[i], t & 31); part[i] = 0.f; }
+      for (int c0 = ch * 8; c0 < C; c0 += GL * 8) {
+        if (!tv) break;
+        float f[8], g[8];
+        ld8(fb + (int64_t)id * C + c0, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = 0.f;
+#pragma unroll
+        for (int i = 0; i < ICT; ++i) {
+          if (ic0 + i >= IC) break;
+          float d[8];
+          ld8(dor + (int64_t)(ic0 + i) * C + c0, d);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            part[i] = fmaf(f[e], d[e], part[i]);
+            g[e] = fmaf(wv[i], d[e], g[e]);
+          }
+        }
+        float* dst = dfb + (int64_t)id * C + c0;
+        red_add_v4(dst, g[0], g[1], g[2], g[3]);
+        red_add_v4(dst + 4, g[4], g[5], g[6], g[7]);
+      }
+#pragma unroll
+      for (int i = 0; i < ICT; ++i) {
+        float sm = part[i];
+#pragma unroll
+        for (int off = 1; off < GL; off <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+        // lane (t & 31) keeps the dot of neighbour t (held by group `slot`)
+        const float got = __shfl_sync(0xffffffffu, sm, ((lane - t0) & (NS - 1)) * GL);
+        if (lane >= t0 && lane < t0 + NS && lane < cnt) my_dw[i] = got;
+      }
+    }
+    if (m < M) {
+#pragma unroll
+      for (int i = 0; i < ICT; ++i)
+        if (ic0 + i < IC) stf(dw + (r * M + m) * IC + ic0 + i, my_dw[i]);
+    }
+  }
+}
+
+template <typename T, int ICT, int GL>
+static void launch_grp(bool bwd, const T* dout, const T* w, const T* feat, const int32_t* idx, int64_t B,
+                       int64_t No, int M, int IC, int ic0, int64_t N, int C, T* out, T* dw, float* dfeat,
+                       cudaStream_t st) {
+  dim3 grid((unsigned)((No + WF_WARPS - 1) / WF_WARPS), (unsigned)B);
+  if (!bwd) wf_fwd_grp_kernel<T, ICT, GL><<<grid, WF_WARPS * 32, 0, st>>>(w, feat, idx, No, M, IC, ic0, N, C, out);
+  else wf_bwd_grp_kernel<T, ICT, GL><<<grid, WF_WARPS * 32, 0, st>>>(dout, w, feat, idx, No, M, IC, ic0, N, C, dw, dfeat);
+}
+
 template <typename T, int ICT>
 static void launch_wf(bool bwd, const T* dout, const T* w, const T* feat, const int32_t* idx,
                       int64_t B, int64_t No, int M, int IC, int ic0, int64_t N, int C, bool vec,
                       T* out, T* dw, float* dfeat, cudaStream_t st) {
+  if (vec) {
+    const int cpl = C / 8;  // 8-channel chunks per row
+    if (cpl <= 4) launch_grp<T, ICT, 4>(bwd, dout, w, feat, idx, B, No, M, IC, ic0, N, C, out, dw, dfeat, st);
+    else if (cpl <= 8) launch_grp<T, ICT, 8>(bwd, dout, w, feat, idx, B, No, M, IC, ic0, N, C, out, dw, dfeat, st);
+    else if (cpl <= 16) launch_grp<T, ICT, 16>(bwd, dout, w, feat, idx, B, No, M, IC, ic0, N, C, out, dw, dfeat, st);
+    else launch_grp<T, ICT, 32>(bwd, dout, w, feat, idx, B, No, M, IC, ic0, N, C, out, dw, dfeat, st);
+    return;
+  }
   dim3 grid((unsigned)((No + WF_WARPS - 1) / WF_WARPS), (unsigned)B);
   dim3 block(WF_WARPS * 32);
-  if (!bwd) {
-    if (vec) wf_fwd_kernel<T, ICT, 8><<<grid, block, 0, st>>>(w, feat, idx, No, M, IC, ic0, N, C, out);
-    else wf_fwd_kernel<T, ICT, 1><<<grid, block, 0, st>>>(w, feat, idx, No, M, IC, ic0, N, C, out);
-  } else {
-    if (vec) wf_bwd_kernel<T, ICT, 8><<<grid, block, 0, st>>>(dout, w, feat, idx, No, M, IC, ic0, N, C, dw, dfeat);
-    else wf_bwd_kernel<T, ICT, 1><<<grid, block, 0, st>>>(dout, w, feat, idx, No, M, IC, ic0, N, C, dw, dfeat);
-  }
+  if (!bwd) wf_fwd_kernel<T, ICT, 1><<<grid, block, 0, st>>>(w, feat, idx, No, M, IC, ic0, N, C, out);
+  else wf_bwd_kernel<T, ICT, 1><<<grid, block, 0, st>>>(dout, w, feat, idx, No, M, IC, ic0, N, C, dw, dfeat);
 }
 
 template <typename T>

@@ -1,12 +1,11 @@
 // Neighbourhood (cluster) attention entry points.
 //
 // Dispatch: 16-bit inputs with head_dim 32 and at most 64 neighbours run on
-// the tensor cores: the cluster-block kernels (nbhd_attn_blk.cu) take every
+// the tensor-core cluster-block kernels (nbhd_attn_blk.cu), which take every
 // 16-query tile whose neighbour lists are runs of 8 consecutive keys (the
-// AFFMAE layout) and list the other tiles, which the neighbour-union kernels
-// (nbhd_attn_tc.cu) then process.  Everything else (fp32, other head dims)
-// runs on the CUDA-core row kernels below (one warp per (b, h, query), see
-// nbhd_row.cuh).
+// AFFMAE layout) and fall back to CUDA-core rows for other tiles.  Everything
+// else (fp32, other head dims) runs on the CUDA-core row kernels below (one
+// warp per (b, h, query), see nbhd_row.cuh).
 #include "nbhd_row.cuh"
 #include "nbhd_tc.cuh"
 
@@ -84,32 +83,16 @@ static NbhdArgs make_args(const void* q, const void* k, const void* v, const int
   return a;
 }
 
-static int tc_prepare(NbhdArgs& a, void* workspace, cudaStream_t st) {
-  AFFB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 15) == 0,
-               "nbhd_attn: a 16-byte aligned workspace of affb_nbhd_attn_workspace_bytes() bytes is required");
-  a.fb_count = (int*)workspace;
-  a.fb_list = (int*)workspace + 4;
-  if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) {
-    set_error("nbhd_attn: workspace reset failed");
-    return AFFB_ERR_CUDA;
-  }
-  return AFFB_OK;
-}
-
 }  // namespace affb
 
 using namespace affb;
-
-extern "C" int64_t affb_nbhd_attn_workspace_bytes(int64_t B, int64_t N) {
-  return nbhd_tc_workspace_bytes(B, N);
-}
 
 extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
                                   const int32_t* member_idx, const void* bias,
                                   const uint8_t* mask, int mask_heads, const void* blank_k,
                                   const void* blank_v, int dtype, int64_t B, int64_t H,
                                   int64_t N, int64_t D, int64_t M, float scale, void* out,
-                                  float* lse, void* workspace, void* stream) {
+                                  float* lse, void* stream) {
   if (int e = check_na(B, H, N, D, M, mask ? mask_heads : 1, blank_k, blank_v, q, k, v)) return e;
   if (B == 0 || N == 0) return AFFB_OK;
   NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, H, N, D, M, scale);
@@ -117,9 +100,7 @@ extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
   a.lse = lse;
   cudaStream_t st = as_stream(stream);
   if (nbhd_tc_supported(dtype, D, M)) {
-    if (int e = tc_prepare(a, workspace, st)) return e;
     if (int e = nbhd_blk_fwd(a, dtype, (int)B, st)) return e;
-    if (int e = nbhd_tc_fwd_list(a, dtype, (int)B, st)) return e;
   } else {
     dim3 grid((unsigned)(((N + NA_WARPS - 1) / NA_WARPS) * B * H));
     AFFB_DISPATCH(dtype, T, dispatch_lpn(D, [&](auto L) {
@@ -137,7 +118,7 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
                                   const void* blank_v, int dtype, int64_t B, int64_t H,
                                   int64_t N, int64_t D, int64_t M, float scale, void* dq,
                                   float* dk_acc, float* dv_acc, void* dbias, float* dbk_acc,
-                                  float* dbv_acc, void* workspace, void* stream) {
+                                  float* dbv_acc, void* stream) {
   if (int e = check_na(B, H, N, D, M, mask ? mask_heads : 1, blank_k, blank_v, q, k, v)) return e;
   AFFB_REQUIRE(!blank_k || (dbk_acc && dbv_acc), "nbhd_attn_bwd: blank gradients need dbk/dbv buffers");
   AFFB_REQUIRE(!bias || dbias, "nbhd_attn_bwd: bias given without a dbias buffer");
@@ -150,9 +131,7 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
   a.dbk = dbk_acc; a.dbv = dbv_acc;
   cudaStream_t st = as_stream(stream);
   if (nbhd_tc_supported(dtype, D, M)) {
-    if (int e = tc_prepare(a, workspace, st)) return e;
     if (int e = nbhd_blk_bwd(a, dtype, (int)B, st)) return e;
-    if (int e = nbhd_tc_bwd_list(a, dtype, (int)B, st)) return e;
   } else {
     dim3 grid((unsigned)(((N + NA_WARPS - 1) / NA_WARPS) * B * H));
     AFFB_DISPATCH(dtype, T, dispatch_lpn(D, [&](auto L) {

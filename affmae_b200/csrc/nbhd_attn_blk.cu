@@ -16,8 +16,8 @@
 //   * K/V rows of a cluster are 512 contiguous bytes per head.
 // Semantics are those of the CUDA-core path (nbhd_row.cuh; reference
 // local_attn.py:224-553).  A tile that is not of this form (or whose cluster
-// union exceeds UCAP/8, or that lists a cluster twice) is appended to a list
-// processed afterwards by the neighbour-union kernels (nbhd_attn_tc.cu).
+// union exceeds UCAP/8, or that lists a cluster twice) runs the CUDA-core row
+// code instead, so any neighbour list stays exact.
 //
 // Per warp and head the work is a flash-attention loop over 16-key chunks
 // (two clusters): S = Q K^T on mma.sync in registers, online softmax in the
@@ -148,10 +148,6 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
   }
   __syncthreads();
   return s.fail ? -1 : total;
-}
-
-__device__ __forceinline__ void push_fallback(const NbhdArgs& a, int tile) {
-  if (threadIdx.x == 0) a.fb_list[atomicAdd(a.fb_count, 1)] = tile;
 }
 
 // Bias pair (columns 8j + 2tq, +1) of row `row` from the staged rows, masked
@@ -306,8 +302,11 @@ __global__ void __launch_bounds__(TC_THREADS) nbhd_blk_fwd_kernel(NbhdArgs a) {
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
   const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
-  if (nclu < 0) { push_fallback(a, blockIdx.x); return; }
   const int warp = threadIdx.x >> 5;
+  if (nclu < 0) {  // not cluster-block lists: CUDA-core rows
+    for (int w = warp; w < a.H * nq; w += NW) nbhd_fwd_row<T, 4>(a, b, w / nq, n0 + w % nq);
+    return;
+  }
   for (int h = warp; h < a.H; h += NW) blk_fwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
 }
 
@@ -447,8 +446,14 @@ __global__ void __launch_bounds__(TC_THREADS) nbhd_blk_bwd_kernel(NbhdArgs a) {
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
   const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
-  if (nclu < 0) { push_fallback(a, blockIdx.x); return; }
   const int warp = threadIdx.x >> 5;
+  if (nclu < 0) {  // not cluster-block lists: CUDA-core rows, blank-token grads straight to global
+    for (int w = warp; w < a.H * nq; w += NW) {
+      const int h = w / nq;
+      nbhd_bwd_row<T, 4>(a, b, h, n0 + w % nq, a.dbk + (int64_t)h * TD, a.dbv + (int64_t)h * TD);
+    }
+    return;
+  }
   for (int h = warp; h < a.H; h += NW) blk_bwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
 }
 

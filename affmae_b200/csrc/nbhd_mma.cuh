@@ -1,8 +1,7 @@
 // Shared building blocks of the tensor-core neighbourhood-attention kernels:
 // mma.sync m16n8k16 (bf16 / fp16 in, fp32 accumulate), ldmatrix fragment
-// loads, cp.async staging and the chunk-level contractions used by both the
-// neighbour-union kernels (nbhd_attn_tc.cu) and the cluster-block kernels
-// (nbhd_attn_blk.cu).
+// loads, cp.async staging and the chunk-level contractions of the
+// cluster-block kernels (nbhd_attn_blk.cu).
 #pragma once
 
 #include "nbhd_row.cuh"
@@ -12,13 +11,9 @@ namespace affb {
 constexpr int TQ = 16;          // queries per tile
 constexpr int TD = 32;          // head dim
 constexpr int MMAX = 64;        // neighbours per query
-constexpr int UCAP = 192;       // max union rows per tile on the tensor-core path
-constexpr int HS = 1024;        // hash slots (>= TQ * MMAX)
+constexpr int UCAP = 192;       // max key rows (union of neighbour clusters) per tile
 constexpr int TC_THREADS = 128;
 constexpr int KST = TD + 8;     // smem row stride (elements) of Q/K/V/dO tiles: 80 B
-constexpr int BST = UCAP + 4;   // fp32 row stride of the bias/slot table
-constexpr int PST = UCAP + 8;   // 16-bit row stride of P / dS tiles
-constexpr int OST = TD + 4;     // fp32 row stride of the cross-warp O / dQ partials
 constexpr int NW = TC_THREADS / 32;
 
 template <typename T> struct MmaType;

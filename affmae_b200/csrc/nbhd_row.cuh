@@ -70,10 +70,6 @@ struct NbhdArgs {
   void* dbias;
   float* dbk;
   float* dbv;
-  // tensor-core path: tiles handed from the cluster-block kernels to the
-  // neighbour-union kernels (count, tile ids)
-  int* fb_count;
-  int* fb_list;
 };
 
 // Forward of one (b, h, n) row by one warp.

@@ -34,11 +34,6 @@ def _prep_mask(mask, B, H, N, M):
     return m, mask.shape[1]
 
 
-def _workspace(B, N, device):
-    n = int(nat.lib().affb_nbhd_attn_workspace_bytes(B, N))
-    return torch.empty(n, dtype=torch.uint8, device=device)
-
-
 def launch_flash_nbhood_attn_fwd(q, k, v, member_index, sm_scale, bias=None, mask=None,
                                  blank_k=None, blank_v=None, exp2=False):
     """Forward: returns (o [B,H,N,D] in q.dtype, lse [B,H,N] fp32)."""
@@ -71,8 +66,7 @@ def launch_flash_nbhood_attn_fwd(q, k, v, member_index, sm_scale, bias=None, mas
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
     nat.call("affb_nbhd_attn_fwd", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(mi), nat.ptr(bias),
              nat.ptr(m8), mh, nat.ptr(blank_k), nat.ptr(blank_v), nat.dcode(q), B, H, N, D, M,
-             float(sm_scale), nat.ptr(o), nat.ptr(lse), nat.ptr(_workspace(B, N, q.device)),
-             nat.stream(q.device))
+             float(sm_scale), nat.ptr(o), nat.ptr(lse), nat.stream(q.device))
     return o, lse
 
 
@@ -116,8 +110,7 @@ def launch_flash_nbhood_attn_bwd(q, k, v, member_index, sm_scale, o, lse, do, bi
              nat.ptr(lse), nat.ptr(mi), nat.ptr(bias), nat.ptr(m8), mh,
              nat.ptr(blank_k) if has_blank else None, nat.ptr(blank_v) if has_blank else None,
              nat.dcode(q), B, H, N, D, M, float(sm_scale), nat.ptr(dq), nat.ptr(dk_acc),
-             nat.ptr(dv_acc), nat.ptr(dbias), nat.ptr(dbk), nat.ptr(dbv),
-             nat.ptr(_workspace(B, N, dev)), nat.stream(dev))
+             nat.ptr(dv_acc), nat.ptr(dbias), nat.ptr(dbk), nat.ptr(dbv), nat.stream(dev))
     dk = nat.cast_from_f32(dk_acc, dt)
     dv = nat.cast_from_f32(dv_acc, dt)
     if has_blank:

@@ -71,28 +71,25 @@ int affb_weighted_features_bwd(const void* dout, const void* w, const void* feat
  * member_idx [B,N,M] int32 (M % 8 == 0); bias [B,H,N,M] T or NULL;
  * mask [B,mask_heads,N,M] uint8 (nonzero = attend) or NULL, mask_heads in {1,H};
  * blank_k, blank_v [H,D] T or NULL (both or neither);
- * out [B,H,N,D] T; lse [B,H,N] fp32.
- * workspace: affb_nbhd_attn_workspace_bytes(B, N) bytes of device memory,
- * 16-byte aligned (contents need no initialisation).                        */
-int64_t affb_nbhd_attn_workspace_bytes(int64_t B, int64_t N);
+ * out [B,H,N,D] T; lse [B,H,N] fp32.                                       */
 int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v, const int32_t* member_idx,
                        const void* bias, const uint8_t* mask, int mask_heads,
                        const void* blank_k, const void* blank_v, int dtype, int64_t B,
                        int64_t H, int64_t N, int64_t D, int64_t M, float scale, void* out,
-                       float* lse, void* workspace, void* stream);
+                       float* lse, void* stream);
 /* Replaces launch_flash_nbhood_attn_bwd (local_attn.py:711).
  * o, dout [B,H,N,D] T; lse [B,H,N] fp32 from the forward.
  * dq [B,H,N,D] T (written); dk_acc, dv_acc [B,H,N,D] fp32 accumulators
  * zeroed by the caller; dbias [B,H,N,M] T (written) or NULL when bias is
  * NULL; dbk_acc, dbv_acc [H,D] fp32 accumulators zeroed by the caller, or
- * NULL when there is no blank token.  workspace as for the forward.         */
+ * NULL when there is no blank token.                                       */
 int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* o,
                        const void* dout, const float* lse, const int32_t* member_idx,
                        const void* bias, const uint8_t* mask, int mask_heads,
                        const void* blank_k, const void* blank_v, int dtype, int64_t B,
                        int64_t H, int64_t N, int64_t D, int64_t M, float scale, void* dq,
                        float* dk_acc, float* dv_acc, void* dbias, float* dbk_acc,
-                       float* dbv_acc, void* workspace, void* stream);
+                       float* dbv_acc, void* stream);
 
 /* ------------------------------------------------ relative-position bias --
  * Replaces the gather of ClusterAttention._make_pos_bias

@@ -42,7 +42,7 @@ def test_argument_errors_are_reported_before_any_launch(lib):
     assert b"exceeds" in lib.affb_last_error()
     with pytest.raises(RuntimeError, match="head_dim"):
         _native.call("affb_nbhd_attn_fwd", None, None, None, None, None, None, 1, None, None, 0,
-                     1, 1, 8, 12, 8, 1.0, None, None, None, None)
+                     1, 1, 8, 12, 8, 1.0, None, None, None)
 
 
 def test_workspace_size_is_monotone(lib):

@@ -279,43 +279,49 @@ def run_gpu(args, world, rank, local):
     achieved = bwd_bytes / (kbwd / 1e3) / 1e9
 
     # ---- e2e through the public autograd API with host buffers
-    host = {n: inp[n].detach().cpu().pin_memory() for n in ("q", "k", "v", "member_idx", "bias", "blank_k",
-                                                             "blank_v", "dout")}
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    def run_e2e():
+        host = {n: inp[n].detach().cpu().pin_memory() for n in ("q", "k", "v", "member_idx", "bias", "blank_k",
+                                                                 "blank_v", "dout")}
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
 
-    outs_host = None
+        outs_host = None
 
-    def e2e_step():
-        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
-        leaves = {n: d[n].requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
-        out = FlashLocalAttentionFunction.apply(leaves["q"], leaves["k"], leaves["v"], d["member_idx"],
-                                                leaves["bias"], None, leaves["blank_k"], leaves["blank_v"], scale)
-        out.backward(d["dout"])
-        res = [out.detach()] + [leaves[n].grad for n in ("q", "k", "v", "bias", "blank_k", "blank_v")]
-        nonlocal outs_host
-        if outs_host is None:  # pinned host buffers for the results, allocated once
-            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-        for hbuf, r in zip(outs_host, res):
-            hbuf.copy_(r, non_blocking=True)
-        return outs_host
+        def e2e_step():
+            d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
+            leaves = {n: d[n].requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
+            out = FlashLocalAttentionFunction.apply(leaves["q"], leaves["k"], leaves["v"], d["member_idx"],
+                                                    leaves["bias"], None, leaves["blank_k"], leaves["blank_v"], scale)
+            out.backward(d["dout"])
+            res = [out.detach()] + [leaves[n].grad for n in ("q", "k", "v", "bias", "blank_k", "blank_v")]
+            nonlocal outs_host
+            if outs_host is None:  # pinned host buffers for the results, allocated once
+                outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+            for hbuf, r in zip(outs_host, res):
+                hbuf.copy_(r, non_blocking=True)
+            return outs_host
 
-    for _ in range(max(1, args.warmup)):
-        outs_host = e2e_step()
-    torch.cuda.synchronize()
-    d2h = sum(t.numel() * t.element_size() for t in outs_host)
-    barrier(world)
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    c = torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(args.steps):
-        outs_host = e2e_step()
-    c.record(stream)
-    torch.cuda.synchronize()
+        for _ in range(max(1, args.warmup)):
+            outs_host = e2e_step()
+        torch.cuda.synchronize()
+        d2h = sum(t.numel() * t.element_size() for t in outs_host)
+        barrier(world)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        c = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            outs_host = e2e_step()
+        c.record(stream)
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(a.elapsed_time(c) / 1e3, world)
+        e2e_value = world * args.steps * (fwd_bytes + bwd_bytes) / e2e_s / 1e9
+        return e2e_value, e2e_s, h2d, d2h
+
+    e2e_value = e2e_s = h2d = d2h = None
+    if not args.no_e2e:
+        e2e_value, e2e_s, h2d, d2h = run_e2e()
     clk.__exit__(None, None, None)
     clocks = clk.summary()
-    e2e_s = max_over_ranks(a.elapsed_time(c) / 1e3, world)
-    e2e_value = world * args.steps * (fwd_bytes + bwd_bytes) / e2e_s / 1e9
 
     # ---- CPU baseline (rank 0, N=1 only): reference formula on one image
     cpu = None
@@ -335,8 +341,9 @@ def run_gpu(args, world, rank, local):
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": workload_config({"parallelism": f"replicas x{world}" if world > 1 else "single GPU"}),
                 "fwd_ms": statistics.median(f_ms), "bwd_ms": statistics.median(b_ms),
-                "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                        "ms_per_step": e2e_s * 1e3 / args.steps},
+                "e2e": None if e2e_value is None else {
+                    "value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_s * 1e3 / args.steps},
                 "roofline": {"kernel": "nbhd_blk_bwd_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
                              "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                              "algorithmic_bytes": bwd_bytes, "kernel_ms": kbwd},
@@ -352,7 +359,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--batch", type=int, default=CFG["B"], help="images per GPU (default: config 3's 32)")
     args = ap.parse_args()
+    CFG["B"] = args.batch
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)

@@ -39,6 +39,8 @@ SIGNATURES = {
     "affb_pos_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "affb_deform_knn_fwd": [_p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p,
                             _p, _p, _p],
+    "affb_deform_knn_fwd_noalloc": [_p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p,
+                                    _p, _p, _p],
     "affb_deform_knn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64,
                             _i64, _p, _p, _p, _p, _p, _p, _p],
     "affb_deform_nbidx_fwd": [_p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i32, _i64,
@@ -52,7 +54,8 @@ SIGNATURES = {
     "affb_mssample_bwd": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p],
     "affb_cast_f32": [_p, _p, _i32, _i64, _p],
 }
-OTHER_SYMBOLS = ["affb_last_error", "affb_abi_version", "affb_deform_workspace_bytes"]
+OTHER_SYMBOLS = ["affb_last_error", "affb_abi_version", "affb_deform_workspace_bytes",
+                 "affb_deform_noalloc_max_scratch_bytes"]
 
 
 def library_path() -> Path:
@@ -78,6 +81,8 @@ def lib():
         l.affb_abi_version.argtypes = []
         l.affb_deform_workspace_bytes.restype = C.c_int64
         l.affb_deform_workspace_bytes.argtypes = [_i64, _i64]
+        l.affb_deform_noalloc_max_scratch_bytes.restype = C.c_int64
+        l.affb_deform_noalloc_max_scratch_bytes.argtypes = []
         for name, args in SIGNATURES.items():
             fn = getattr(l, name)
             fn.argtypes = args

@@ -15,6 +15,9 @@
 
 #include "../../include/affmae_b200.h"
 
+// Size of the fixed device scratch of affb_deform_knn_fwd_noalloc.
+#define AFFB_NOALLOC_SCRATCH_BYTES (16u << 20)
+
 namespace affb {
 
 // ---------------------------------------------------------------- errors --

@@ -25,6 +25,8 @@
 // caller-provided workspace by four small kernels (bbox, count, scan, scatter).
 #include "deform_grid.cuh"
 
+#include <mutex>
+
 namespace affb {
 
 constexpr int DK_WARPS = 8;
@@ -442,4 +444,67 @@ extern "C" int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos,
                     d_kvpos, d_values_acc, d_power));
   AFFB_LAUNCH_CHECK("affb_deform_knn_bwd");
   return AFFB_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Allocation-free variant of affb_deform_knn_fwd.
+//
+// The spatial grid lives in a fixed, file-scope device array instead of a
+// caller-provided workspace.  Every GPU that loads this library reserves the
+// array (AFFB_NOALLOC_SCRATCH_BYTES) for the life of the process.  Host code
+// must not hand the array's name to a kernel: on the host it only stands for
+// the symbol, so its device address is fetched once per device with
+// cudaGetSymbolAddress (with that device current) and cached.
+namespace affb {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[AFFB_NOALLOC_SCRATCH_BYTES];
+
+static void* noalloc_scratch_address(int dev, int* err) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  *err = AFFB_OK;
+  if (dev < 0 || dev >= 64) { *err = AFFB_ERR_INVALID; return nullptr; }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (rc != cudaSuccess || p == nullptr) {
+      set_error("deform_knn_fwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(rc));
+      *err = AFFB_ERR_CUDA;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+}  // namespace affb
+
+extern "C" int64_t affb_deform_noalloc_max_scratch_bytes(void) { return AFFB_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int affb_deform_knn_fwd_noalloc(const float* query_pos, const float* kv_pos,
+                                           const float* offsets, const float* attn_w,
+                                           const void* values, const float* power, int dtype,
+                                           int64_t B, int64_t Nq, int64_t Nkv, int64_t H, int64_t C,
+                                           void* out, int32_t* knn_idx, float* knn_d2,
+                                           void* stream) {
+  if (int e = check_deform(B, Nq, Nkv, H, C)) return e;
+  const int64_t need = grid_layout(B, Nkv).total;
+  AFFB_REQUIRE(need <= (int64_t)AFFB_NOALLOC_SCRATCH_BYTES,
+               "deform_knn_fwd_noalloc: B=%lld x Nkv=%lld needs %lld bytes of grid scratch; the fixed "
+               "scratch holds %lld bytes (use affb_deform_knn_fwd with a workspace instead)",
+               (long long)B, (long long)Nkv, (long long)need, (long long)AFFB_NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_error("deform_knn_fwd_noalloc: no current CUDA device");
+    return AFFB_ERR_CUDA;
+  }
+  int err = AFFB_OK;
+  void* scratch = noalloc_scratch_address(dev, &err);
+  if (err != AFFB_OK) return err;
+  // The grid build clears its cell counters on every call, so the scratch
+  // keeps no state that a later call depends on.
+  return affb_deform_knn_fwd(query_pos, kv_pos, offsets, attn_w, values, power, dtype, B, Nq, Nkv, H,
+                             C, out, knn_idx, knn_d2, scratch, stream);
 }

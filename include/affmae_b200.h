@@ -123,6 +123,30 @@ int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos, const float
                         int dtype, int64_t B, int64_t Nq, int64_t Nkv, int64_t H, int64_t C,
                         void* out, int32_t* knn_idx, float* knn_d2, void* workspace,
                         void* stream);
+/* Allocation-free variant of affb_deform_knn_fwd; it has no counterpart in
+ * the reference.  For callers that may not allocate device memory on the
+ * call path: hosts whose device memory is owned by another allocator (a
+ * framework's caching allocator, an inference engine's memory pool or a
+ * plugin interface that only hands over input/output buffers), where a
+ * cudaMalloc would synchronise the device and bypass the owner's budget.
+ * Same arguments and results as affb_deform_knn_fwd minus `workspace`: the
+ * spatial grid is built in a fixed device array of
+ * affb_deform_noalloc_max_scratch_bytes() bytes (16 MiB) that every GPU
+ * loading the library holds until the process exits.  Sizes whose grid
+ * (affb_deform_workspace_bytes(B, Nkv)) exceeds it are rejected with an
+ * error.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and caches it, so make that first call before any
+ * stream capture.  Every call on a device shares that device's array, which
+ * keeps the last call's contents (each call clears what it needs cleared);
+ * calls whose GPU work can overlap (for example on unordered streams) race
+ * on it and must be serialised by the caller.                              */
+int64_t affb_deform_noalloc_max_scratch_bytes(void);
+int affb_deform_knn_fwd_noalloc(const float* query_pos, const float* kv_pos,
+                                const float* offsets, const float* attn_w, const void* values,
+                                const float* power, int dtype, int64_t B, int64_t Nq,
+                                int64_t Nkv, int64_t H, int64_t C, void* out, int32_t* knn_idx,
+                                float* knn_d2, void* stream);
+
 /* Replaces fused_knn_deform_cross_attn_backward (fused_deform_attn.py:2792)
  * and fused_knn_deform_self_attn_backward (:2661).  dout [B,Nq,H,C] T.
  * Written: d_offsets [B,Nq,H,4,2] fp32, d_attn_w [B,Nq,H,4] fp32.

@@ -6,8 +6,8 @@
 // is tokens [8c, 8c+8) (BasicLayer.forward, src/layers/aff.py:445-453;
 // space_filling_cluster, src/utils/geometry.py:314-317).  Each list is then
 // M/8 runs idx[8j .. 8j+7] = 8c_j + (0..7).  This kernel exploits that:
-//   * per tile of 16 queries the union is a set of clusters (<= UCAP/8),
-//     found by hashing the M/8 cluster ids of each row (not M keys);
+//   * per tile of 16 queries the union is a set of at most 16 * M/8
+//     clusters, found by hashing the M/8 cluster ids of each row (not M keys);
 //   * one mma n-tile (8 columns) is exactly one cluster, so the attended
 //     pattern is a [16 x clusters] table of list positions j (or absent),
 //     shared by all heads; bias[q, 8j + r] is read straight from the staged
@@ -15,8 +15,8 @@
 //     accumulator fragments;
 //   * K/V rows of a cluster are 512 contiguous bytes per head.
 // Semantics are those of the CUDA-core path (nbhd_row.cuh; reference
-// local_attn.py:224-553).  A tile that is not of this form (or whose cluster
-// union exceeds UCAP/8, or that lists a cluster twice) runs the CUDA-core row
+// local_attn.py:224-553).  A tile that is not of this form (or that lists a
+// cluster twice in one row) runs the CUDA-core row
 // code instead, so any neighbour list stays exact.
 //
 // Per warp and head the work is a flash-attention loop over 16-key chunks
@@ -28,14 +28,14 @@
 
 namespace affb {
 
-constexpr int UCLU = UCAP / 8;   // clusters per tile on this path
+constexpr int UCLU = TQ * MMAX / 8;  // clusters per tile: every row's list, all distinct
 constexpr int CHS = 256;         // cluster hash slots
 constexpr int BPT = 24;          // 16-bit row stride of the per-warp 16x16 P / dS tiles
 
 struct BlkSetup {
   alignas(16) int idx[TQ * MMAX];  // staged neighbour rows
-  int ukey[UCAP];                  // key rows of the cluster union (8 per cluster)
-  int jtab[TQ][UCLU];              // list position j of cluster slot u in row q, -1 absent
+  int uclu[UCLU];                  // cluster ids of the union (key rows 8c .. 8c+7)
+  int8_t jtab[TQ][UCLU];           // list position j of cluster slot u in row q, -1 absent
   int hkey[CHS], hval[CHS];
   int warp_tot[NW];
   int nclu, fail;
@@ -84,7 +84,7 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
     cp_commit();
   }
   for (int i = t; i < CHS; i += TC_THREADS) s.hkey[i] = -1;
-  for (int i = t; i < TQ * UCLU; i += TC_THREADS) (&s.jtab[0][0])[i] = -1;
+  for (int i = t; i < TQ * UCLU / 4; i += TC_THREADS) reinterpret_cast<int*>(&s.jtab[0][0])[i] = -1;
   if (t == 0) s.fail = 0;
   cp_wait<0>();
   __syncthreads();
@@ -97,6 +97,7 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
     bool ok = c0 >= 0 && (c0 & 7) == 0 && c0 + 8 <= N;
 #pragma unroll
     for (int r = 1; r < 8; ++r) ok = ok && run[r] == c0 + r;
+    for (int jj = 0; jj < j; ++jj) ok = ok && s.idx[q * M + 8 * jj] != c0;  // listed twice in one row
     if (ok) {
       cid = c0 >> 3;
       uint32_t h = clu_slot(cid);
@@ -128,15 +129,13 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
     if (i < w) base += s.warp_tot[i];
     total += s.warp_tot[i];
   }
-  if (total > UCLU) return -1;
   int pos = base + x - c;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int key = s.hkey[2 * t + i];
     if (key >= 0) {
       s.hval[2 * t + i] = pos;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) s.ukey[pos * 8 + r] = key * 8 + r;
+      s.uclu[pos] = key;
       ++pos;
     }
   }
@@ -144,10 +143,10 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
   if (cid >= 0) {
     uint32_t h = clu_slot(cid);
     while (s.hkey[h] != cid) h = (h + 1) & (CHS - 1);
-    if (atomicExch(&s.jtab[q][s.hval[h]], j) != -1) s.fail = 1;  // cluster listed twice in a row
+    s.jtab[q][s.hval[h]] = (int8_t)j;  // one writer per slot: duplicates were rejected above
   }
   __syncthreads();
-  return s.fail ? -1 : total;
+  return total;
 }
 
 // Bias pair (columns 8j + 2tq, +1) of row `row` from the staged rows, masked
@@ -180,8 +179,10 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
   const int64_t bh = (int64_t)b * a.H + h;
   const T* kb = (const T*)a.k + bh * N * TD;
   const T* vb = (const T*)a.v + bh * N * TD;
-  const int* ukey = s.ukey;
-  auto rows_u = [&](int u0) { return [=](int i) -> int64_t { return u0 + i < U ? ukey[u0 + i] : -1; }; };
+  const int* uclu = s.uclu;
+  auto rows_u = [&](int u0) {
+    return [=](int i) -> int64_t { return u0 + i < U ? (int64_t)uclu[(u0 + i) >> 3] * 8 + ((u0 + i) & 7) : -1; };
+  };
   warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, [=](int i) -> int64_t { return i < nq ? i : -1; });
   if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
   cp_commit();
@@ -319,8 +320,10 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
   const int64_t bh = (int64_t)b * a.H + h;
   const T* kb = (const T*)a.k + bh * N * TD;
   const T* vb = (const T*)a.v + bh * N * TD;
-  const int* ukey = s.ukey;
-  auto rows_u = [&](int u0) { return [=](int i) -> int64_t { return u0 + i < U ? ukey[u0 + i] : -1; }; };
+  const int* uclu = s.uclu;
+  auto rows_u = [&](int u0) {
+    return [=](int i) -> int64_t { return u0 + i < U ? (int64_t)uclu[(u0 + i) >> 3] * 8 + ((u0 + i) & 7) : -1; };
+  };
   auto rows_q = [=](int i) -> int64_t { return i < nq ? i : -1; };
   warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, rows_q);
   warp_load16(w.dO, (const T*)a.dout + (bh * N + n0) * TD, rows_q);
@@ -416,8 +419,8 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
                             pack2<T>(ds[1][0], ds[1][1]), pack2<T>(ds[1][2], ds[1][3])};
     mma_chunk_pv<T>(qacc, da, w.KV[buf][0], 0);
     __syncwarp();
-    mma_chunk_scatter<T>(w.dS, BPT, w.Q, ukey, U, c * 16, a.scale, a.dk + bh * N * TD);
-    mma_chunk_scatter<T>(w.P, BPT, w.dO, ukey, U, c * 16, 1.f, a.dv + bh * N * TD);
+    mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD);
+    mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD);
     __syncwarp();
   }
   const T* bkp = a.blank_k ? (const T*)a.blank_k + (int64_t)h * TD : nullptr;

@@ -11,7 +11,6 @@ namespace affb {
 constexpr int TQ = 16;          // queries per tile
 constexpr int TD = 32;          // head dim
 constexpr int MMAX = 64;        // neighbours per query
-constexpr int UCAP = 192;       // max key rows (union of neighbour clusters) per tile
 constexpr int TC_THREADS = 128;
 constexpr int KST = TD + 8;     // smem row stride (elements) of Q/K/V/dO tiles: 80 B
 constexpr int NW = TC_THREADS / 32;
@@ -106,10 +105,10 @@ __device__ __forceinline__ void mma_chunk_pv(float (*out)[4], const uint32_t* a,
 }
 
 // Scatter-add of R[16 x 32] = Pt[0..15][0..15]^T (16 x 16, row stride pst) *
-// Y[16 x 32] (times `mul`) into rows ukey[u0 + i] of dst (fp32, row stride
-// TD) for u0 + i < U.
+// Y[16 x 32] (times `mul`) into key rows 8 * uclu[u >> 3] + (u & 7), u = u0 + i,
+// of dst (fp32, row stride TD) for u < U.
 template <typename T>
-__device__ __forceinline__ void mma_chunk_scatter(const T* Pt, int pst, const T* Y, const int* ukey, int U,
+__device__ __forceinline__ void mma_chunk_scatter(const T* Pt, int pst, const T* Y, const int* uclu, int U,
                                                   int u0, float mul, float* __restrict__ dst) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
@@ -125,8 +124,8 @@ __device__ __forceinline__ void mma_chunk_scatter(const T* Pt, int pst, const T*
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     MmaType<T>::mma(acc, a, yb);
     const int col = nt * 8 + 2 * tq;
-    if (ua < U) red_add_v2(dst + (int64_t)ukey[ua] * TD + col, acc[0] * mul, acc[1] * mul);
-    if (ub < U) red_add_v2(dst + (int64_t)ukey[ub] * TD + col, acc[2] * mul, acc[3] * mul);
+    if (ua < U) red_add_v2(dst + ((int64_t)uclu[ua >> 3] * 8 + (ua & 7)) * TD + col, acc[0] * mul, acc[1] * mul);
+    if (ub < U) red_add_v2(dst + ((int64_t)uclu[ub >> 3] * 8 + (ub & 7)) * TD + col, acc[2] * mul, acc[3] * mul);
   }
 }
 

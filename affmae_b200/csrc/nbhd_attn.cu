@@ -111,32 +111,78 @@ extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
   return AFFB_OK;
 }
 
+// fp32 runs the CUDA-core kernels straight into dk / dv; everything else
+// needs fp32 sums (and the tensor-core path its inverse lists).
+static NbhdBwdLayout bwd_layout(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, int64_t M,
+                                unsigned char* base) {
+  const bool tc = nbhd_tc_supported(dtype, D, M);
+  return nbhd_bwd_layout(tc, tc || dtype != AFFB_F32, B, H, N, D, M, base);
+}
+
+extern "C" int64_t affb_nbhd_attn_bwd_workspace_bytes(int dtype, int64_t B, int64_t H, int64_t N,
+                                                       int64_t D, int64_t M) {
+  if (B < 0 || H < 0 || N < 0 || D < 0 || M < 0) return -1;
+  return (int64_t)bwd_layout(dtype, B, H, N, D, M, nullptr).total;
+}
+
 extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* o,
                                   const void* dout, const float* lse,
                                   const int32_t* member_idx, const void* bias,
                                   const uint8_t* mask, int mask_heads, const void* blank_k,
                                   const void* blank_v, int dtype, int64_t B, int64_t H,
                                   int64_t N, int64_t D, int64_t M, float scale, void* dq,
-                                  float* dk_acc, float* dv_acc, void* dbias, float* dbk_acc,
-                                  float* dbv_acc, void* stream) {
+                                  void* dk, void* dv, void* dbias, float* dbk_acc,
+                                  float* dbv_acc, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
   if (int e = check_na(B, H, N, D, M, mask ? mask_heads : 1, blank_k, blank_v, q, k, v)) return e;
   AFFB_REQUIRE(!blank_k || (dbk_acc && dbv_acc), "nbhd_attn_bwd: blank gradients need dbk/dbv buffers");
   AFFB_REQUIRE(!bias || dbias, "nbhd_attn_bwd: bias given without a dbias buffer");
-  AFFB_REQUIRE(((uintptr_t)dk_acc | (uintptr_t)dv_acc | (uintptr_t)o | (uintptr_t)dout | (uintptr_t)dq) % 16 == 0,
-               "nbhd_attn_bwd: o/dout/dq/dk/dv buffers must be 16-byte aligned");
+  AFFB_REQUIRE(((uintptr_t)dk | (uintptr_t)dv | (uintptr_t)o | (uintptr_t)dout | (uintptr_t)dq |
+                (uintptr_t)member_idx) % 16 == 0,
+               "nbhd_attn_bwd: o/dout/dq/dk/dv/member_idx buffers must be 16-byte aligned");
+  AFFB_REQUIRE((uintptr_t)workspace % 256 == 0, "nbhd_attn_bwd: workspace must be 256-byte aligned");
+  const NbhdBwdLayout ly = bwd_layout(dtype, B, H, N, D, M, (unsigned char*)workspace);
+  AFFB_REQUIRE(workspace_bytes >= (int64_t)ly.total,
+               "nbhd_attn_bwd: workspace of %lld bytes, %lld needed (affb_nbhd_attn_bwd_workspace_bytes)",
+               (long long)workspace_bytes, (long long)ly.total);
+  AFFB_REQUIRE(ly.total == 0 || workspace, "nbhd_attn_bwd: workspace is NULL");
   if (B == 0 || N == 0) return AFFB_OK;
+  AFFB_REQUIRE(B * N * (M / 8) < (1ll << 31), "nbhd_attn_bwd: too many list entries");
   NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, H, N, D, M, scale);
   a.o = o; a.dout = dout; a.lse = const_cast<float*>(lse);
-  a.dq = dq; a.dk = dk_acc; a.dv = dv_acc; a.dbias = bias ? dbias : nullptr;
+  a.dq = dq; a.dbias = bias ? dbias : nullptr;
   a.dbk = dbk_acc; a.dbv = dbv_acc;
   cudaStream_t st = as_stream(stream);
+  const int64_t nel = B * H * N * D;
   if (nbhd_tc_supported(dtype, D, M)) {
+    a.dk = ly.acc_k; a.dv = ly.acc_v;
+    a.general = ly.flag;
+    a.di = ly.di;
+    KvArgs kv{};
+    kv.flag = ly.flag; kv.counts = ly.counts; kv.offs = ly.offs; kv.entries = ly.entries;
+    kv.di = ly.di; kv.acc_k = ly.acc_k; kv.acc_v = ly.acc_v;
+    kv.dk = dk; kv.dv = dv;
+    kv.Cc = (int)((N + 7) / 8);
+    if (int e = nbhd_inv_lists(a, kv, ly, (int)B, st)) return e;
     if (int e = nbhd_blk_bwd(a, dtype, (int)B, st)) return e;
+    if (int e = nbhd_kv_bwd(a, kv, dtype, (int)B, st)) return e;
   } else {
+    float* sk = dtype == AFFB_F32 ? (float*)dk : ly.acc_k;
+    float* sv = dtype == AFFB_F32 ? (float*)dv : ly.acc_v;
+    if (cudaMemsetAsync(sk, 0, nel * sizeof(float), st) != cudaSuccess ||
+        cudaMemsetAsync(sv, 0, nel * sizeof(float), st) != cudaSuccess) {
+      set_error("nbhd_attn_bwd: cudaMemsetAsync failed");
+      return AFFB_ERR_CUDA;
+    }
+    a.dk = sk; a.dv = sv;
     dim3 grid((unsigned)(((N + NA_WARPS - 1) / NA_WARPS) * B * H));
     AFFB_DISPATCH(dtype, T, dispatch_lpn(D, [&](auto L) {
       nbhd_attn_bwd_kernel<T, decltype(L)::value><<<grid, NA_WARPS * 32, 0, st>>>(a);
     }));
+    if (dtype != AFFB_F32) {
+      if (int e = affb_cast_f32(sk, dk, dtype, nel, stream)) return e;
+      if (int e = affb_cast_f32(sv, dv, dtype, nel, stream)) return e;
+    }
   }
   AFFB_LAUNCH_CHECK("affb_nbhd_attn_bwd");
   return AFFB_OK;

@@ -22,7 +22,9 @@
 // Per warp and head the work is a flash-attention loop over 16-key chunks
 // (two clusters): S = Q K^T on mma.sync in registers, online softmax in the
 // accumulator layout, O += P V.  The backward recomputes S and dP = dO V^T,
-// keeps dQ in registers, and scatters dK = dS^T Q, dV = P^T dO per chunk.
+// keeps dQ in registers and writes dbias; dK and dV come from the key-major
+// pass of nbhd_attn_kv.cu, unless the call's lists are not all cluster runs,
+// in which case dK = dS^T Q and dV = P^T dO are scatter-added per chunk.
 #include "nbhd_tc.cuh"
 #include "nbhd_mma.cuh"
 
@@ -311,7 +313,9 @@ __global__ void __launch_bounds__(TC_THREADS) nbhd_blk_fwd_kernel(NbhdArgs a) {
   for (int h = warp; h < a.H; h += NW) blk_fwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
 }
 
-template <typename T>
+// SCATTER: also scatter-add dK / dV into the fp32 sums a.dk / a.dv (lists not
+// all cluster runs); otherwise write D = rowsum(O * dO) for the key side.
+template <typename T, bool SCATTER>
 __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>& w, int b, int h, int n0,
                              int nq, int nclu) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
@@ -350,6 +354,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
     p += __shfl_xor_sync(0xffffffffu, p, 1);
     p += __shfl_xor_sync(0xffffffffu, p, 2);
     dl[hf] = p;
+    if (!SCATTER && tq == 0 && row < nq) a.di[bh * N + n0 + row] = p;
   }
   cp_wait<1>();
   __syncwarp();
@@ -411,17 +416,21 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
         const uint32_t dpk = pack2<T>(ds[nt][2 * hf], ds[nt][2 * hf + 1]);
         if (dbase && jv >= 0 && row < nq)
           *reinterpret_cast<uint32_t*>(dbase + row * M + 8 * jv + 2 * tq) = dpk;
-        *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
-        *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);
+        if (SCATTER) {
+          *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
+          *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);
+        }
       }
     }
     const uint32_t da[4] = {pack2<T>(ds[0][0], ds[0][1]), pack2<T>(ds[0][2], ds[0][3]),
                             pack2<T>(ds[1][0], ds[1][1]), pack2<T>(ds[1][2], ds[1][3])};
     mma_chunk_pv<T>(qacc, da, w.KV[buf][0], 0);
     __syncwarp();
-    mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD);
-    mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD);
-    __syncwarp();
+    if (SCATTER) {
+      mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD);
+      mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD);
+      __syncwarp();
+    }
   }
   const T* bkp = a.blank_k ? (const T*)a.blank_k + (int64_t)h * TD : nullptr;
 #pragma unroll
@@ -457,7 +466,11 @@ __global__ void __launch_bounds__(TC_THREADS) nbhd_blk_bwd_kernel(NbhdArgs a) {
     }
     return;
   }
-  for (int h = warp; h < a.H; h += NW) blk_bwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  if (*a.general) {
+    for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, true>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  } else {
+    for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, false>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  }
 }
 
 template <typename K>

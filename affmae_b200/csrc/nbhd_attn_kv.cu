@@ -1,0 +1,376 @@
+// Backward of the cluster-block neighbourhood attention, key side: dK and dV
+// computed key-major from inverse neighbour lists, with no atomics and no
+// fp32 accumulators.
+//
+// The reference accumulates dK / dV by atomically adding each query's
+// contribution into fp32 buffers (local_attn.py:518-519, tl.atomic_add on
+// DK / DV).  Here the lists are inverted once per call instead:
+//   inv_count  one thread per query: checks that its list is M/8 runs of 8
+//              consecutive keys starting at a multiple of 8 with no cluster
+//              listed twice (the same test as the query-side tile setup),
+//              counts the queries that list each key cluster and remembers
+//              the rank of every (query, run) entry;
+//   inv_scan   one block per image: exclusive scan of the counts;
+//   inv_fill   writes entry q * 8 + j (query q lists the cluster as run j)
+//              at its slot of the cluster's list.
+// A call whose lists are not all of that form sets a flag instead; the
+// query-side kernel then scatter-adds dK / dV into fp32 buffers as before
+// (inv_fill zeroes them) and nbhd_kv_kernel converts them to the output type.
+//
+// nbhd_kv_kernel: one block per key cluster (8 keys), one warp per head.
+// The cluster's list is sorted by query in shared memory (so the summation
+// order, and the result, is deterministic); the warp walks it in chunks of 16
+// queries, gathering their Q / dO rows, lse, D = rowsum(O * dO), bias run and
+// mask run with cp.async, and computes on the tensor cores
+//   S  = Q_c K^T,  dP = dO_c V^T            (16 queries x 8 keys)
+//   P  = exp(S * scale + bias - lse),  dS = P (dP - D)
+//   dV^T += dO_c^T P,  dK^T += Q_c^T dS      (32 dims x 8 keys)
+// P and dS become the B operands of the last two products with one
+// movmatrix.trans per 8x8 block.  Every computed (query, key) pair is a
+// listed one, so no work is spent on masked pairs.
+#include "nbhd_tc.cuh"
+#include "nbhd_mma.cuh"
+
+namespace affb {
+
+constexpr int KV_LCAP = 512;  // lists up to this length are sorted in shared memory
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 4 : 0));
+}
+
+// ---------------------------------------------------------------- lists --
+
+__global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, int N, int M, int Cc,
+                                      int* __restrict__ flag, int* __restrict__ counts,
+                                      int* __restrict__ ecl, int* __restrict__ erk) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (int64_t)B * N) return;
+  const int b = (int)(t / N);
+  const int J = M >> 3;
+  const int4* row = reinterpret_cast<const int4*>(midx + t * M);
+  int cs[8];
+  bool ok = true;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    cs[j] = -1;
+    if (j < J) {
+      const int4 x = __ldg(row + 2 * j), y = __ldg(row + 2 * j + 1);
+      const int c0 = x.x;
+      ok = ok && c0 >= 0 && (c0 & 7) == 0 && c0 <= N - 8 && x.y == c0 + 1 && x.z == c0 + 2 &&
+           x.w == c0 + 3 && y.x == c0 + 4 && y.y == c0 + 5 && y.z == c0 + 6 && y.w == c0 + 7;
+      cs[j] = c0 >> 3;
+#pragma unroll
+      for (int jj = 0; jj < j; ++jj) ok = ok && cs[jj] != cs[j];
+    }
+  }
+  if (!ok) {
+    *reinterpret_cast<volatile int*>(flag) = 1;
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j < J) {
+      ecl[t * J + j] = cs[j];
+      erk[t * J + j] = atomicAdd(counts + (int64_t)b * Cc + cs[j], 1);
+    }
+  }
+}
+
+// Exclusive scan of one image's cluster counts; slots of image b start at
+// b * N * J (every query has exactly J entries).
+__global__ void __launch_bounds__(1024) nbhd_inv_scan_kernel(const int* __restrict__ counts, int N, int J,
+                                                             int Cc, const int* __restrict__ flag,
+                                                             int* __restrict__ offs) {
+  __shared__ int wsum[32];
+  __shared__ int carry_s;
+  if (*flag) return;
+  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int* cnt = counts + (int64_t)b * Cc;
+  int* off = offs + (int64_t)b * Cc;
+  if (t == 0) carry_s = 0;
+  __syncthreads();
+  for (int base = 0; base < Cc; base += 1024) {
+    const int v = base + t < Cc ? cnt[base + t] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int s = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      wsum[lane] = s;  // inclusive over warps
+    }
+    __syncthreads();
+    const int carry = carry_s;
+    const int excl = carry + (w ? wsum[w - 1] : 0) + x - v;
+    if (base + t < Cc) off[base + t] = (int)((int64_t)b * N * J) + excl;
+    __syncthreads();
+    if (t == 0) carry_s = carry + wsum[31];
+    __syncthreads();
+  }
+}
+
+__global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const int* __restrict__ flag,
+                                     const int* __restrict__ offs, const int* __restrict__ ecl,
+                                     const int* __restrict__ erk, int* __restrict__ entries,
+                                     float* __restrict__ acc_k, float* __restrict__ acc_v) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (int64_t)B * N) return;
+  const int b = (int)(t / N), q = (int)(t % N);
+  if (*flag) {  // general lists: the query side scatter-adds into zeroed fp32 buffers
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int h = 0; h < H; ++h) {
+      float4* pk = reinterpret_cast<float4*>(acc_k + (((int64_t)b * H + h) * N + q) * TD);
+      float4* pv = reinterpret_cast<float4*>(acc_v + (((int64_t)b * H + h) * N + q) * TD);
+#pragma unroll
+      for (int i = 0; i < TD / 4; ++i) { pk[i] = z; pv[i] = z; }
+    }
+    return;
+  }
+  const int J = M >> 3;
+  for (int j = 0; j < J; ++j) {
+    const int c = ecl[t * J + j];
+    entries[offs[(int64_t)b * Cc + c] + erk[t * J + j]] = q * 8 + j;
+  }
+}
+
+// ------------------------------------------------------ key-major pass --
+
+template <typename T>
+struct KvWarp {
+  alignas(16) T K[8 * KST];
+  alignas(16) T V[8 * KST];
+  alignas(16) T Q[2][16 * KST];
+  alignas(16) T dO[2][16 * KST];
+  alignas(16) T bias[2][16 * 8];
+  alignas(16) uint8_t mask[2][16 * 8];
+  alignas(16) float lse[2][16];
+  alignas(16) float di[2][16];
+  alignas(16) T ost[8 * KST];
+};
+template <typename T>
+struct KvSmem {
+  int list[KV_LCAP];
+  int tmp[KV_LCAP];
+  KvWarp<T> w[NW];
+};
+
+// Gathers chunk rows base .. base+15 of list L (n entries) into stage `buf`.
+template <typename T>
+__device__ __forceinline__ void kv_stage(const NbhdArgs& a, const KvArgs& k, KvWarp<T>& w, const int* L, int n,
+                                         int base, int buf, int b, int h) {
+  const int lane = threadIdx.x & 31;
+  const int N = a.N, M = a.M;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const int nr = n - base;
+#pragma unroll
+  for (int i = lane; i < 64; i += 32) {
+    const int row = i >> 2, piece = i & 3;
+    const bool valid = row < nr;
+    const int q = valid ? (L[base + row] >> 3) : 0;
+    cp_async16(w.Q[buf] + row * KST + piece * 8, (const T*)a.q + (bh * N + q) * TD + piece * 8, valid);
+    cp_async16(w.dO[buf] + row * KST + piece * 8, (const T*)a.dout + (bh * N + q) * TD + piece * 8, valid);
+  }
+  const int row = lane & 15;
+  const bool valid = row < nr;
+  const int e = valid ? L[base + row] : 0;
+  const int q = e >> 3, j = e & 7;
+  if (lane < 16) {
+    if (a.bias) cp_async16(w.bias[buf] + row * 8, (const T*)a.bias + (bh * N + q) * M + 8 * j, valid);
+    cp_async4(&w.lse[buf][row], a.lse + bh * N + q, valid);
+  } else {
+    if (a.mask) {
+      const int64_t mh = a.mask_heads == 1 ? 0 : h;
+      cp_async8(w.mask[buf] + row * 8, a.mask + (((int64_t)b * a.mask_heads + mh) * N + q) * M + 8 * j, valid);
+    }
+    cp_async4(&w.di[buf][row], k.di + bh * N + q, valid);
+  }
+}
+
+template <typename T>
+__device__ void kv_head(const NbhdArgs& a, const KvArgs& k, KvWarp<T>& w, const int* L, int n, int b, int h,
+                        int c) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int N = a.N;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const int kr0 = 8 * c, nkeys = min(8, N - kr0);
+  float dkt[2][4], dvt[2][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dkt[i][e] = dvt[i][e] = 0.f;
+  if (n > 0) {
+    {
+      const int row = lane >> 2, piece = lane & 3;
+      const bool valid = row < nkeys;
+      const int64_t src = (bh * N + kr0 + (valid ? row : 0)) * TD + piece * 8;
+      cp_async16(w.K + row * KST + piece * 8, (const T*)a.k + src, valid);
+      cp_async16(w.V + row * KST + piece * 8, (const T*)a.v + src, valid);
+    }
+    kv_stage<T>(a, k, w, L, n, 0, 0, b, h);
+    cp_commit();
+    const int nch = (n + 15) >> 4;
+    uint32_t bk[4], bv[4];
+    for (int ch = 0; ch < nch; ++ch) {
+      const int buf = ch & 1;
+      if (ch + 1 < nch) kv_stage<T>(a, k, w, L, n, (ch + 1) * 16, buf ^ 1, b, h);
+      cp_commit();
+      cp_wait<1>();
+      __syncwarp();
+      if (ch == 0) {
+        ldsm_x4(bk, w.K + (lane & 7) * KST + (lane >> 3) * 8);
+        ldsm_x4(bv, w.V + (lane & 7) * KST + (lane >> 3) * 8);
+      }
+      uint32_t aq[2][4], ado[2][4];
+      load_a_frags(aq, w.Q[buf]);
+      load_a_frags(ado, w.dO[buf]);
+      float s[4] = {0.f, 0.f, 0.f, 0.f}, dp[4] = {0.f, 0.f, 0.f, 0.f};
+      MmaType<T>::mma(s, aq[0], bk);
+      MmaType<T>::mma(s, aq[1], bk + 2);
+      MmaType<T>::mma(dp, ado[0], bv);
+      MmaType<T>::mma(dp, ado[1], bv + 2);
+      const int nr = n - ch * 16;
+      uint32_t pp[2], pd[2];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = g + 8 * hf;
+        const float ls = w.lse[buf][row], dd = w.di[buf][row];
+        float b0 = 0.f, b1 = 0.f;
+        if (a.bias) {
+          const uint32_t u = *reinterpret_cast<const uint32_t*>(w.bias[buf] + row * 8 + 2 * tq);
+          const T* hp = reinterpret_cast<const T*>(&u);
+          b0 = io<T>::ld(hp);
+          b1 = io<T>::ld(hp + 1);
+        }
+        bool v0 = row < nr, v1 = v0;
+        if (a.mask) {
+          v0 = v0 && w.mask[buf][row * 8 + 2 * tq] != 0;
+          v1 = v1 && w.mask[buf][row * 8 + 2 * tq + 1] != 0;
+        }
+        const float p0 = v0 ? __expf(s[2 * hf] * a.scale + b0 - ls) : 0.f;
+        const float p1 = v1 ? __expf(s[2 * hf + 1] * a.scale + b1 - ls) : 0.f;
+        pp[hf] = pack2<T>(p0, p1);
+        pd[hf] = pack2<T>(p0 * (dp[2 * hf] - dd), p1 * (dp[2 * hf + 1] - dd));
+      }
+      const uint32_t bp[2] = {movmatrix_t(pp[0]), movmatrix_t(pp[1])};
+      const uint32_t bd[2] = {movmatrix_t(pd[0]), movmatrix_t(pd[1])};
+      const int mi = lane >> 3;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        // A[m = dim][k = query] = X[query][dim]: matrices (d 0-7, q 0-7), (d 8-15, q 0-7), (d 0-7, q 8-15), (d 8-15, q 8-15)
+        const int off = ((mi >> 1) * 8 + (lane & 7)) * KST + (mt * 2 + (mi & 1)) * 8;
+        uint32_t ad[4], aqt[4];
+        ldsm_x4_t(ad, w.dO[buf] + off);
+        ldsm_x4_t(aqt, w.Q[buf] + off);
+        MmaType<T>::mma(dvt[mt], ad, bp);
+        MmaType<T>::mma(dkt[mt], aqt, bd);
+      }
+      __syncwarp();
+    }
+  }
+  // transpose through shared memory and store 16-byte pieces of the key rows
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const float(*acc)[4] = pass == 0 ? dkt : dvt;
+    const float mul = pass == 0 ? a.scale : 1.f;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = mt * 16 + g + (e >> 1) * 8, key = 2 * tq + (e & 1);
+        io<T>::st(w.ost + key * KST + d, acc[mt][e] * mul);
+      }
+    __syncwarp();
+    const int row = lane >> 2, piece = lane & 3;
+    if (row < nkeys) {
+      T* dst = (T*)(pass == 0 ? k.dk : k.dv) + (bh * N + kr0 + row) * TD + piece * 8;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(w.ost + row * KST + piece * 8);
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS) nbhd_kv_kernel(NbhdArgs a, KvArgs k) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  KvSmem<T>& s = *reinterpret_cast<KvSmem<T>*>(smem_raw);
+  const int N = a.N, Cc = k.Cc;
+  const int b = blockIdx.x / Cc, c = blockIdx.x % Cc;
+  const int t = threadIdx.x, warp = t >> 5;
+  if (*k.flag) {  // general lists: convert the fp32 sums of the query side
+    const int nkeys = min(8, N - 8 * c);
+    const int per_head = nkeys * TD;
+    for (int i = t; i < a.H * per_head; i += TC_THREADS) {
+      const int h = i / per_head, r = i % per_head;
+      const int64_t o = (((int64_t)b * a.H + h) * N + 8 * c) * TD + r;
+      io<T>::st((T*)k.dk + o, k.acc_k[o]);
+      io<T>::st((T*)k.dv + o, k.acc_v[o]);
+    }
+    return;
+  }
+  const int64_t cell = (int64_t)b * Cc + c;
+  const int n = k.counts[cell];
+  const int* src = k.entries + k.offs[cell];
+  const int* L = src;
+  if (n <= KV_LCAP) {  // rank sort by query (entries are distinct)
+    for (int i = t; i < n; i += TC_THREADS) s.tmp[i] = src[i];
+    __syncthreads();
+    for (int i = t; i < n; i += TC_THREADS) {
+      const int e = s.tmp[i];
+      int r = 0;
+      for (int m = 0; m < n; ++m) r += s.tmp[m] < e;
+      s.list[r] = e;
+    }
+    __syncthreads();
+    L = s.list;
+  }
+  for (int h = warp; h < a.H; h += NW) kv_head<T>(a, k, s.w[warp], L, n, b, h, c);
+}
+
+int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st) {
+  const int64_t blocks = (int64_t)B * k.Cc;
+  if (blocks == 0) return AFFB_OK;
+  AFFB_REQUIRE(blocks < (1ll << 31), "nbhd_attn_bwd: too many key clusters");
+  auto go = [&](auto kernel, size_t smem) -> int {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      set_error("nbhd_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
+      return AFFB_ERR_CUDA;
+    }
+    kernel<<<(unsigned)blocks, TC_THREADS, smem, st>>>(a, k);
+    return AFFB_OK;
+  };
+  if (dtype == AFFB_BF16) return go(nbhd_kv_kernel<__nv_bfloat16>, sizeof(KvSmem<__nv_bfloat16>));
+  return go(nbhd_kv_kernel<__half>, sizeof(KvSmem<__half>));
+}
+
+int nbhd_inv_lists(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, int B, cudaStream_t st) {
+  const int N = a.N, M = a.M, Cc = k.Cc;
+  const int64_t rows = (int64_t)B * N;
+  if (cudaMemsetAsync(ly.flag, 0, ly.zero_bytes, st) != cudaSuccess) {
+    set_error("nbhd_attn_bwd: cudaMemsetAsync failed");
+    return AFFB_ERR_CUDA;
+  }
+  const unsigned g = (unsigned)((rows + 255) / 256);
+  nbhd_inv_count_kernel<<<g, 256, 0, st>>>(a.midx, B, N, M, Cc, ly.flag, ly.counts, ly.ecl, ly.erk);
+  nbhd_inv_scan_kernel<<<B, 1024, 0, st>>>(ly.counts, N, M >> 3, Cc, ly.flag, ly.offs);
+  nbhd_inv_fill_kernel<<<g, 256, 0, st>>>(B, N, M, Cc, a.H, ly.flag, ly.offs, ly.ecl, ly.erk, ly.entries,
+                                          ly.acc_k, ly.acc_v);
+  return AFFB_OK;
+}
+
+}  // namespace affb

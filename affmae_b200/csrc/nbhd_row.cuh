@@ -70,6 +70,10 @@ struct NbhdArgs {
   void* dbias;
   float* dbk;
   float* dbv;
+  // cluster-block backward: list-form flag (nonzero: dK / dV are scatter-added
+  // into dk / dv by the query side) and D = rowsum(O * dO) per (b, h, n)
+  const int* general;
+  float* di;
 };
 
 // Forward of one (b, h, n) row by one warp.

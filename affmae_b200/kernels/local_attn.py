@@ -9,7 +9,7 @@ Differences that are deliberate:
     under autocast and rounds O through fp16 even for fp32 inputs;
   * a [B,1,N,M] mask is read per batch element instead of being expanded to
     [B,H,N,M];
-  * O and dQ are written directly, without zero-initialised fp32 buffers.
+  * O, dQ, dK and dV are written directly, without zero-initialised fp32 buffers.
 """
 from __future__ import annotations
 
@@ -101,18 +101,19 @@ def launch_flash_nbhood_attn_bwd(q, k, v, member_index, sm_scale, o, lse, do, bi
     m8, mh = _prep_mask(mask, B, H, N, M)
     dev = q.device
     dq = torch.empty_like(q)
-    dk_acc = torch.zeros((B, H, N, D), device=dev, dtype=torch.float32)
-    dv_acc = torch.zeros((B, H, N, D), device=dev, dtype=torch.float32)
+    dk = torch.empty_like(q)
+    dv = torch.empty_like(q)
     dbias = torch.empty((B, H, N, M), device=dev, dtype=dt) if has_bias else None
     dbk = torch.zeros((H, D), device=dev, dtype=torch.float32) if has_blank else None
     dbv = torch.zeros((H, D), device=dev, dtype=torch.float32) if has_blank else None
+    wsb = int(nat.lib().affb_nbhd_attn_bwd_workspace_bytes(nat.dcode(q), B, H, N, D, M))
+    ws = torch.empty((max(wsb, 1),), device=dev, dtype=torch.uint8)
     nat.call("affb_nbhd_attn_bwd", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(o), nat.ptr(do),
              nat.ptr(lse), nat.ptr(mi), nat.ptr(bias), nat.ptr(m8), mh,
              nat.ptr(blank_k) if has_blank else None, nat.ptr(blank_v) if has_blank else None,
-             nat.dcode(q), B, H, N, D, M, float(sm_scale), nat.ptr(dq), nat.ptr(dk_acc),
-             nat.ptr(dv_acc), nat.ptr(dbias), nat.ptr(dbk), nat.ptr(dbv), nat.stream(dev))
-    dk = nat.cast_from_f32(dk_acc, dt)
-    dv = nat.cast_from_f32(dv_acc, dt)
+             nat.dcode(q), B, H, N, D, M, float(sm_scale), nat.ptr(dq), nat.ptr(dk),
+             nat.ptr(dv), nat.ptr(dbias), nat.ptr(dbk), nat.ptr(dbv), nat.ptr(ws), wsb,
+             nat.stream(dev))
     if has_blank:
         dbk = dbk.to(dt)
         dbv = dbv.to(dt)

@@ -79,17 +79,21 @@ int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v, const int32_
                        float* lse, void* stream);
 /* Replaces launch_flash_nbhood_attn_bwd (local_attn.py:711).
  * o, dout [B,H,N,D] T; lse [B,H,N] fp32 from the forward.
- * dq [B,H,N,D] T (written); dk_acc, dv_acc [B,H,N,D] fp32 accumulators
- * zeroed by the caller; dbias [B,H,N,M] T (written) or NULL when bias is
- * NULL; dbk_acc, dbv_acc [H,D] fp32 accumulators zeroed by the caller, or
- * NULL when there is no blank token.                                       */
+ * dq, dk, dv [B,H,N,D] T (written); dbias [B,H,N,M] T (written) or NULL
+ * when bias is NULL; dbk_acc, dbv_acc [H,D] fp32 accumulators zeroed by the
+ * caller, or NULL when there is no blank token.  workspace: device memory of
+ * at least affb_nbhd_attn_bwd_workspace_bytes(...) bytes, 256-byte aligned,
+ * no initial contents (the reference allocates its fp32 dK / dV buffers
+ * itself, local_attn.py:785-787).  member_idx 16-byte aligned.            */
+int64_t affb_nbhd_attn_bwd_workspace_bytes(int dtype, int64_t B, int64_t H, int64_t N,
+                                           int64_t D, int64_t M);
 int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* o,
                        const void* dout, const float* lse, const int32_t* member_idx,
                        const void* bias, const uint8_t* mask, int mask_heads,
                        const void* blank_k, const void* blank_v, int dtype, int64_t B,
                        int64_t H, int64_t N, int64_t D, int64_t M, float scale, void* dq,
-                       float* dk_acc, float* dv_acc, void* dbias, float* dbk_acc,
-                       float* dbv_acc, void* stream);
+                       void* dk, void* dv, void* dbias, float* dbk_acc, float* dbv_acc,
+                       void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------ relative-position bias --
  * Replaces the gather of ClusterAttention._make_pos_bias

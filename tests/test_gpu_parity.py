@@ -432,3 +432,59 @@ def test_local_attn_mixed_block_and_general_tiles(cuda):
                                lse.cpu(), inp["dout"].cpu(), **cpu)
     for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
         assert rel_err(a.cpu(), b) < TOL_LP, name
+
+
+@pytest.mark.gpu
+def test_local_attn_key_major_long_and_empty_lists(cuda):
+    """Key clusters listed by more queries than fit the shared-memory sort (unsorted
+    path), clusters listed by nobody and a partial last cluster (N % 8 != 0): dK and
+    dV of the key-major pass."""
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    B, H, N, D, M = 1, 4, 1029, 32, 64
+    inp = _attn_inputs(B, H, N, D, M, torch.bfloat16, seed=11)
+    gen = torch.Generator().manual_seed(12)
+    runs = torch.stack([torch.randperm(10, generator=gen)[:8] for _ in range(N)])  # clusters 0..9
+    inp["mi"] = (runs[:, :, None] * 8 + torch.arange(8)).reshape(1, N, M).to(torch.int32)
+    G = _to(inp, cuda)
+    kw = lambda d: dict(bias=d["bias"], mask=d["mask"], blank_k=d["blank_k"], blank_v=d["blank_v"])
+    o, lse = launch_flash_nbhood_attn_fwd(G["q"], G["k"], G["v"], G["mi"], 32 ** -0.5, **kw(G))
+    grads = launch_flash_nbhood_attn_bwd(G["q"], G["k"], G["v"], G["mi"], 32 ** -0.5, o, lse, G["do"], **kw(G))
+    ref = oracle.nbhd_attn_bwd(inp["q"], inp["k"], inp["v"], inp["mi"], 32 ** -0.5, o.cpu(), lse.cpu(), inp["do"],
+                               **kw(inp))
+    for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
+        assert rel_err(a.cpu(), b) < TOL_LP, name
+    assert torch.count_nonzero(grads[1][:, :, 80:]) == 0 and torch.count_nonzero(grads[2][:, :, 80:]) == 0
+
+
+@pytest.mark.gpu
+def test_local_attn_backward_deterministic(cuda):
+    """Sorted inverse lists and no atomics on dQ/dK/dV: two calls agree bit for bit."""
+    from affmae_b200.workloads import nbhd_attention_inputs
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    inp = nbhd_attention_inputs(B=2, side=48, H=4, dtype=torch.bfloat16, seed=4, device=cuda)
+    kw = dict(bias=inp["bias"], blank_k=inp["blank_k"], blank_v=inp["blank_v"])
+    o, lse = launch_flash_nbhood_attn_fwd(inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["scale"], **kw)
+    g1 = launch_flash_nbhood_attn_bwd(inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["scale"], o, lse,
+                                      inp["dout"], **kw)
+    g2 = launch_flash_nbhood_attn_bwd(inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["scale"], o, lse,
+                                      inp["dout"], **kw)
+    for name, a, b in zip(["dq", "dk", "dv", "dbias"], g1[:4], g2[:4]):
+        assert torch.equal(a, b), name
+
+
+@pytest.mark.gpu
+def test_nbhd_bwd_workspace_checked(cuda):
+    """The C entry point rejects a workspace below affb_nbhd_attn_bwd_workspace_bytes."""
+    from affmae_b200 import _native as nat
+    B, H, N, D, M = 1, 2, 64, 32, 16
+    need = int(nat.lib().affb_nbhd_attn_bwd_workspace_bytes(nat.BF16, B, H, N, D, M))
+    assert need > 0
+    t = torch.zeros((B, H, N, D), device=cuda, dtype=torch.bfloat16)
+    lse = torch.zeros((B, H, N), device=cuda)
+    mi = torch.zeros((B, N, M), device=cuda, dtype=torch.int32)
+    ws = torch.empty((need,), device=cuda, dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="workspace"):
+        nat.call("affb_nbhd_attn_bwd", t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(),
+                 lse.data_ptr(), mi.data_ptr(), None, None, 1, None, None, nat.BF16, B, H, N, D, M, 1.0,
+                 t.data_ptr(), t.data_ptr(), t.data_ptr(), None, None, None, ws.data_ptr(), need - 1,
+                 nat.stream(t.device))

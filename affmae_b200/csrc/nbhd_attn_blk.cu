@@ -33,11 +33,13 @@ namespace affb {
 constexpr int UCLU = TQ * MMAX / 8;  // clusters per tile: every row's list, all distinct
 constexpr int CHS = 256;         // cluster hash slots
 constexpr int BPT = 24;          // 16-bit row stride of the per-warp 16x16 P / dS tiles
+constexpr int BSENT = TQ * MMAX; // offset of the -inf block that ends each staged bias tile
 
 struct BlkSetup {
   alignas(16) int idx[TQ * MMAX];  // staged neighbour rows
   int uclu[UCLU];                  // cluster ids of the union (key rows 8c .. 8c+7)
-  int8_t jtab[TQ][UCLU];           // list position j of cluster slot u in row q, -1 absent
+  int16_t boff[TQ][UCLU];          // row q, cluster slot u: offset q*M + 8j of its bias run in the
+                                   // staged tile (list position j), BSENT when q does not list it
   int hkey[CHS], hval[CHS];
   int warp_tot[NW];
   int nclu, fail;
@@ -46,14 +48,14 @@ struct BlkSetup {
 template <typename T>
 struct BlkWarpFwd {
   alignas(16) T Q[TQ * KST];
-  alignas(16) T bias[TQ * MMAX];
+  alignas(16) T bias[TQ * MMAX + 8];
   alignas(16) T KV[2][2][16 * KST];
 };
 template <typename T>
 struct BlkWarpBwd {
   alignas(16) T Q[TQ * KST];
   alignas(16) T dO[TQ * KST];
-  alignas(16) T bias[TQ * MMAX];
+  alignas(16) T bias[TQ * MMAX + 8];
   alignas(16) T KV[2][2][16 * KST];
   alignas(16) T P[TQ * BPT];
   alignas(16) T dS[TQ * BPT];
@@ -86,7 +88,8 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
     cp_commit();
   }
   for (int i = t; i < CHS; i += TC_THREADS) s.hkey[i] = -1;
-  for (int i = t; i < TQ * UCLU / 4; i += TC_THREADS) reinterpret_cast<int*>(&s.jtab[0][0])[i] = -1;
+  for (int i = t; i < TQ * UCLU / 2; i += TC_THREADS)
+    reinterpret_cast<int*>(&s.boff[0][0])[i] = BSENT | (BSENT << 16);
   if (t == 0) s.fail = 0;
   cp_wait<0>();
   __syncthreads();
@@ -145,30 +148,53 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
   if (cid >= 0) {
     uint32_t h = clu_slot(cid);
     while (s.hkey[h] != cid) h = (h + 1) & (CHS - 1);
-    s.jtab[q][s.hval[h]] = (int8_t)j;  // one writer per slot: duplicates were rejected above
+    s.boff[q][s.hval[h]] = (int16_t)(q * M + 8 * j);  // one writer per slot: duplicates rejected above
   }
   __syncthreads();
   return total;
 }
 
-// Bias pair (columns 8j + 2tq, +1) of row `row` from the staged rows, masked
-// entries (mask == 0) and absent clusters giving -inf.
+// Staged bias tile of one warp: rows [16][M] of bias (zeros without bias),
+// -inf where the mask is 0, and the -inf block at BSENT for absent clusters.
+// Called once the bias cp.async group has completed.
 template <typename T>
-__device__ __forceinline__ void bias_pair(const NbhdArgs& a, const T* sbias, const uint8_t* mrow, int M, int row,
-                                          int jv, int tq, float& b0, float& b1) {
-  if (jv < 0) { b0 = b1 = -INFINITY; return; }
-  const int col = 8 * jv + 2 * tq;
-  if (a.bias) {
-    const uint32_t u = *reinterpret_cast<const uint32_t*>(sbias + row * M + col);
-    const T* hp = reinterpret_cast<const T*>(&u);
-    b0 = io<T>::ld(hp);
-    b1 = io<T>::ld(hp + 1);
-  } else {
-    b0 = b1 = 0.f;
+__device__ __forceinline__ void warp_finish_bias(T* sb, const NbhdArgs& a, const uint8_t* mrow, int nq) {
+  const int lane = threadIdx.x & 31, M = a.M;
+  const T ninf = neg_inf<T>();
+  if (!a.bias) {
+    const T zero = pos_zero<T>();
+    for (int i = lane; i < TQ * M; i += 32) sb[i] = zero;
   }
-  if (mrow) {
-    if (mrow[row * M + col] == 0) b0 = -INFINITY;
-    if (mrow[row * M + col + 1] == 0) b1 = -INFINITY;
+  if (mrow)
+    for (int i = lane; i < nq * M; i += 32)
+      if (mrow[i] == 0) sb[i] = ninf;
+  if (lane < 8) sb[BSENT + lane] = ninf;
+  __syncwarp();
+}
+
+// Bias pair at tile offset bo (columns 2tq, 2tq+1 of the run).
+template <typename T>
+__device__ __forceinline__ void bias_at(const T* sb, int bo, int tq, float& b0, float& b1) {
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(sb + bo + 2 * tq);
+  const T* hp = reinterpret_cast<const T*>(&u);
+  b0 = io<T>::ld(hp);
+  b1 = io<T>::ld(hp + 1);
+}
+
+// cp.async of the K and V rows of cluster slots 2c, 2c+1 (16 keys), zeros past nclu.
+template <typename T>
+__device__ __forceinline__ void warp_load_kv(T* dk, T* dv, const T* __restrict__ kb, const T* __restrict__ vb,
+                                             const int* uclu, int c, int nclu) {
+  const int lane = threadIdx.x & 31;
+  const int r = lane >> 2, piece = lane & 3;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int u = 2 * c + hh;
+    const bool ok = u < nclu;
+    const int64_t src = (int64_t)(ok ? uclu[u] * 8 + r : 0) * TD + piece * 8;
+    const int dst = (hh * 8 + r) * KST + piece * 8;
+    cp_async16(dk + dst, kb + src, ok);
+    cp_async16(dv + dst, vb + src, ok);
   }
 }
 
@@ -177,19 +203,15 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
                              int nq, int nclu) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int N = a.N, M = a.M;
-  const int U = nclu * 8, nchunk = (nclu + 1) / 2;
+  const int nchunk = (nclu + 1) / 2;
   const int64_t bh = (int64_t)b * a.H + h;
   const T* kb = (const T*)a.k + bh * N * TD;
   const T* vb = (const T*)a.v + bh * N * TD;
   const int* uclu = s.uclu;
-  auto rows_u = [&](int u0) {
-    return [=](int i) -> int64_t { return u0 + i < U ? (int64_t)uclu[(u0 + i) >> 3] * 8 + ((u0 + i) & 7) : -1; };
-  };
   warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, [=](int i) -> int64_t { return i < nq ? i : -1; });
   if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
   cp_commit();
-  warp_load16(w.KV[0][0], kb, rows_u(0));
-  warp_load16(w.KV[0][1], vb, rows_u(0));
+  warp_load_kv(w.KV[0][0], w.KV[0][1], kb, vb, uclu, 0, nclu);
   cp_commit();
   const uint8_t* mrow = a.mask ? a.mask + (((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N + n0) * M : nullptr;
   int ex[2] = {0, 0};
@@ -207,6 +229,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
   }
   cp_wait<1>();
   __syncwarp();
+  warp_finish_bias(w.bias, a, mrow, nq);
   uint32_t aq[2][4];
   load_a_frags(aq, w.Q);
   float sbv[2] = {-INFINITY, -INFINITY};
@@ -221,10 +244,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
   for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   for (int c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
-    if (c + 1 < nchunk) {
-      warp_load16(w.KV[buf ^ 1][0], kb, rows_u((c + 1) * 16));
-      warp_load16(w.KV[buf ^ 1][1], vb, rows_u((c + 1) * 16));
-    }
+    if (c + 1 < nchunk) warp_load_kv(w.KV[buf ^ 1][0], w.KV[buf ^ 1][1], kb, vb, uclu, c + 1, nclu);
     cp_commit();
     cp_wait<1>();
     __syncwarp();
@@ -237,7 +257,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
       for (int hf = 0; hf < 2; ++hf) {
         const int row = g + hf * 8;
         float b0, b1;
-        bias_pair<T>(a, w.bias, mrow, M, row, s.jtab[row][2 * c + nt], tq, b0, b1);
+        bias_at(w.bias, s.boff[row][2 * c + nt], tq, b0, b1);
         x[nt][2 * hf] = x[nt][2 * hf] * a.scale + b0;
         x[nt][2 * hf + 1] = x[nt][2 * hf + 1] * a.scale + b1;
         cm[hf] = fmaxf(cm[hf], fmaxf(x[nt][2 * hf], x[nt][2 * hf + 1]));
@@ -325,16 +345,12 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
   const T* kb = (const T*)a.k + bh * N * TD;
   const T* vb = (const T*)a.v + bh * N * TD;
   const int* uclu = s.uclu;
-  auto rows_u = [&](int u0) {
-    return [=](int i) -> int64_t { return u0 + i < U ? (int64_t)uclu[(u0 + i) >> 3] * 8 + ((u0 + i) & 7) : -1; };
-  };
   auto rows_q = [=](int i) -> int64_t { return i < nq ? i : -1; };
   warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, rows_q);
   warp_load16(w.dO, (const T*)a.dout + (bh * N + n0) * TD, rows_q);
   if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
   cp_commit();
-  warp_load16(w.KV[0][0], kb, rows_u(0));
-  warp_load16(w.KV[0][1], vb, rows_u(0));
+  warp_load_kv(w.KV[0][0], w.KV[0][1], kb, vb, uclu, 0, nclu);
   cp_commit();
   const uint8_t* mrow = a.mask ? a.mask + (((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N + n0) * M : nullptr;
   float dl[2], ls[2];
@@ -358,6 +374,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
   }
   cp_wait<1>();
   __syncwarp();
+  warp_finish_bias(w.bias, a, mrow, nq);
   uint32_t aq[2][4], ado[2][4];
   load_a_frags(aq, w.Q);
   load_a_frags(ado, w.dO);
@@ -389,10 +406,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
   for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
   for (int c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
-    if (c + 1 < nchunk) {
-      warp_load16(w.KV[buf ^ 1][0], kb, rows_u((c + 1) * 16));
-      warp_load16(w.KV[buf ^ 1][1], vb, rows_u((c + 1) * 16));
-    }
+    if (c + 1 < nchunk) warp_load_kv(w.KV[buf ^ 1][0], w.KV[buf ^ 1][1], kb, vb, uclu, c + 1, nclu);
     cp_commit();
     cp_wait<1>();
     __syncwarp();
@@ -406,16 +420,15 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int row = g + hf * 8;
-        const int jv = s.jtab[row][2 * c + nt];
+        const int bo = s.boff[row][2 * c + nt];
         float b0, b1;
-        bias_pair<T>(a, w.bias, mrow, M, row, jv, tq, b0, b1);
+        bias_at(w.bias, bo, tq, b0, b1);
         p[nt][2 * hf] = __expf(sx[nt][2 * hf] * a.scale + b0 - ls[hf]);
         p[nt][2 * hf + 1] = __expf(sx[nt][2 * hf + 1] * a.scale + b1 - ls[hf]);
         ds[nt][2 * hf] = p[nt][2 * hf] * (dp[nt][2 * hf] - dl[hf]);
         ds[nt][2 * hf + 1] = p[nt][2 * hf + 1] * (dp[nt][2 * hf + 1] - dl[hf]);
         const uint32_t dpk = pack2<T>(ds[nt][2 * hf], ds[nt][2 * hf + 1]);
-        if (dbase && jv >= 0 && row < nq)
-          *reinterpret_cast<uint32_t*>(dbase + row * M + 8 * jv + 2 * tq) = dpk;
+        if (dbase && bo != BSENT && row < nq) *reinterpret_cast<uint32_t*>(dbase + bo + 2 * tq) = dpk;
         if (SCATTER) {
           *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
           *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);

@@ -140,6 +140,9 @@ __device__ __forceinline__ void load_a_frags(uint32_t (*a)[4], const T* A) {
 template <typename T> __device__ __forceinline__ T neg_inf();
 template <> __device__ __forceinline__ __nv_bfloat16 neg_inf<__nv_bfloat16>() { return __ushort_as_bfloat16(0xFF80); }
 template <> __device__ __forceinline__ __half neg_inf<__half>() { return __ushort_as_half(0xFC00); }
+template <typename T> __device__ __forceinline__ T pos_zero();
+template <> __device__ __forceinline__ __nv_bfloat16 pos_zero<__nv_bfloat16>() { return __ushort_as_bfloat16(0); }
+template <> __device__ __forceinline__ __half pos_zero<__half>() { return __ushort_as_half(0); }
 
 // cp.async of 16 rows (64 B each): rows src + rowidx(i) * TD for valid i, zeros otherwise.
 template <typename T, typename RowOf>

@@ -155,17 +155,22 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
   cudaStream_t st = as_stream(stream);
   const int64_t nel = B * H * N * D;
   if (nbhd_tc_supported(dtype, D, M)) {
+    // lists -> prologue (D, blank terms) -> [query side, only for lists that
+    // are not all cluster runs] -> key side (dK, dV, dS) -> dQ from dS
     a.dk = ly.acc_k; a.dv = ly.acc_v;
     a.general = ly.flag;
-    a.di = ly.di;
     KvArgs kv{};
     kv.flag = ly.flag; kv.counts = ly.counts; kv.offs = ly.offs; kv.entries = ly.entries;
-    kv.di = ly.di; kv.acc_k = ly.acc_k; kv.acc_v = ly.acc_v;
+    kv.di = ly.di; kv.dsb = ly.dsb; kv.ds = bias ? dbias : ly.ds;
+    kv.acc_k = ly.acc_k; kv.acc_v = ly.acc_v;
     kv.dk = dk; kv.dv = dv;
     kv.Cc = (int)((N + 7) / 8);
+    a.ds = kv.ds; a.dsb = ly.dsb;
     if (int e = nbhd_inv_lists(a, kv, ly, (int)B, st)) return e;
+    if (int e = nbhd_q_prologue(a, kv, dtype, (int)B, st)) return e;
     if (int e = nbhd_blk_bwd(a, dtype, (int)B, st)) return e;
     if (int e = nbhd_kv_bwd(a, kv, dtype, (int)B, st)) return e;
+    if (int e = nbhd_blk_dq(a, dtype, (int)B, st)) return e;
   } else {
     float* sk = dtype == AFFB_F32 ? (float*)dk : ly.acc_k;
     float* sv = dtype == AFFB_F32 ? (float*)dv : ly.acc_v;

@@ -61,6 +61,11 @@ struct BlkWarpBwd {
   alignas(16) T dS[TQ * BPT];
 };
 template <typename T>
+struct BlkWarpDq {
+  alignas(16) T dS[TQ * MMAX + 8];
+  alignas(16) T K[2][16 * KST];
+};
+template <typename T>
 struct BlkFwdSmem {
   BlkSetup setup;
   BlkWarpFwd<T> w[NW];
@@ -69,6 +74,11 @@ template <typename T>
 struct BlkBwdSmem {
   BlkSetup setup;
   BlkWarpBwd<T> w[NW];
+};
+template <typename T>
+struct BlkDqSmem {
+  BlkSetup setup;
+  BlkWarpDq<T> w[NW];
 };
 
 __device__ __forceinline__ uint32_t clu_slot(int key) { return ((uint32_t)key * 2654435761u) >> 24; }
@@ -179,6 +189,20 @@ __device__ __forceinline__ void bias_at(const T* sb, int bo, int tq, float& b0, 
   const T* hp = reinterpret_cast<const T*>(&u);
   b0 = io<T>::ld(hp);
   b1 = io<T>::ld(hp + 1);
+}
+
+// cp.async of the K rows of cluster slots 2c, 2c+1 (16 keys), zeros past nclu.
+template <typename T>
+__device__ __forceinline__ void warp_load_k(T* dk, const T* __restrict__ kb, const int* uclu, int c, int nclu) {
+  const int lane = threadIdx.x & 31;
+  const int r = lane >> 2, piece = lane & 3;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int u = 2 * c + hh;
+    const bool ok = u < nclu;
+    const int64_t src = (int64_t)(ok ? uclu[u] * 8 + r : 0) * TD + piece * 8;
+    cp_async16(dk + (hh * 8 + r) * KST + piece * 8, kb + src, ok);
+  }
 }
 
 // cp.async of the K and V rows of cluster slots 2c, 2c+1 (16 keys), zeros past nclu.
@@ -316,7 +340,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
 }
 
 template <typename T>
-__global__ void __launch_bounds__(TC_THREADS) nbhd_blk_fwd_kernel(NbhdArgs a) {
+__global__ void __launch_bounds__(TC_THREADS, AFFB_FWD_MINB) nbhd_blk_fwd_kernel(NbhdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlkFwdSmem<T>& s = *reinterpret_cast<BlkFwdSmem<T>*>(smem_raw);
   const int N = a.N;
@@ -333,9 +357,10 @@ __global__ void __launch_bounds__(TC_THREADS) nbhd_blk_fwd_kernel(NbhdArgs a) {
   for (int h = warp; h < a.H; h += NW) blk_fwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
 }
 
-// SCATTER: also scatter-add dK / dV into the fp32 sums a.dk / a.dv (lists not
-// all cluster runs); otherwise write D = rowsum(O * dO) for the key side.
-template <typename T, bool SCATTER>
+// Full backward of one head for calls whose lists are not all cluster runs:
+// dQ, dbias and the blank-token gradients, with dK / dV scatter-added into
+// the fp32 sums a.dk / a.dv.
+template <typename T>
 __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>& w, int b, int h, int n0,
                              int nq, int nclu) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
@@ -370,7 +395,6 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
     p += __shfl_xor_sync(0xffffffffu, p, 1);
     p += __shfl_xor_sync(0xffffffffu, p, 2);
     dl[hf] = p;
-    if (!SCATTER && tq == 0 && row < nq) a.di[bh * N + n0 + row] = p;
   }
   cp_wait<1>();
   __syncwarp();
@@ -429,21 +453,17 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
         ds[nt][2 * hf + 1] = p[nt][2 * hf + 1] * (dp[nt][2 * hf + 1] - dl[hf]);
         const uint32_t dpk = pack2<T>(ds[nt][2 * hf], ds[nt][2 * hf + 1]);
         if (dbase && bo != BSENT && row < nq) *reinterpret_cast<uint32_t*>(dbase + bo + 2 * tq) = dpk;
-        if (SCATTER) {
-          *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
-          *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);
-        }
+        *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
+        *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);
       }
     }
     const uint32_t da[4] = {pack2<T>(ds[0][0], ds[0][1]), pack2<T>(ds[0][2], ds[0][3]),
                             pack2<T>(ds[1][0], ds[1][1]), pack2<T>(ds[1][2], ds[1][3])};
     mma_chunk_pv<T>(qacc, da, w.KV[buf][0], 0);
     __syncwarp();
-    if (SCATTER) {
-      mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD);
-      mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD);
-      __syncwarp();
-    }
+    mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD);
+    mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD);
+    __syncwarp();
   }
   const T* bkp = a.blank_k ? (const T*)a.blank_k + (int64_t)h * TD : nullptr;
 #pragma unroll
@@ -461,8 +481,11 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
   }
 }
 
+// Only for calls whose lists are not all cluster runs (flag set by the list
+// builder); otherwise the key-side and dQ kernels do the backward.
 template <typename T>
-__global__ void __launch_bounds__(TC_THREADS) nbhd_blk_bwd_kernel(NbhdArgs a) {
+__global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel(NbhdArgs a) {
+  if (!*a.general) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlkBwdSmem<T>& s = *reinterpret_cast<BlkBwdSmem<T>*>(smem_raw);
   const int N = a.N;
@@ -479,11 +502,85 @@ __global__ void __launch_bounds__(TC_THREADS) nbhd_blk_bwd_kernel(NbhdArgs a) {
     }
     return;
   }
-  if (*a.general) {
-    for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, true>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
-  } else {
-    for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, false>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  for (int h = warp; h < a.H; h += NW) blk_bwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+}
+
+// dQ of one head and tile from dS, which the key-side kernel has written in
+// bias layout ([B,H,N,M], a.ds):  dQ = scale * (sum_j dS[q, 8j+r] K[key] +
+// ds_blank[q] blank_k).  The A fragments of each 16-key chunk are read from
+// the staged dS rows through the bias-run offset table (absent clusters hit a
+// zero block), so a chunk is two 32-bit loads per fragment half and four mma.
+template <typename T>
+__device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpDq<T>& w, int b, int h, int n0,
+                            int nq, int nclu) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int N = a.N, M = a.M;
+  const int nchunk = (nclu + 1) / 2;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const T* kb = (const T*)a.k + bh * N * TD;
+  {
+    const T* src = (const T*)a.ds + (bh * N + n0) * M;
+    const int nch = TQ * M / 8;
+    for (int i = lane; i < nch; i += 32) {
+      const bool ok = (i * 8) / M < nq;
+      cp_async16(w.dS + i * 8, src + (ok ? i * 8 : 0), ok);
+    }
   }
+  cp_commit();
+  warp_load_k(w.K[0], kb, s.uclu, 0, nclu);
+  cp_commit();
+  if (lane < 8) w.dS[BSENT + lane] = pos_zero<T>();
+  float qacc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
+  for (int c = 0; c < nchunk; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunk) warp_load_k(w.K[buf ^ 1], kb, s.uclu, c + 1, nclu);
+    cp_commit();
+    cp_wait<1>();
+    __syncwarp();
+    uint32_t da[4];
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int bo = s.boff[g + 8 * hf][2 * c + kh];
+        da[kh * 2 + hf] = *reinterpret_cast<const uint32_t*>(w.dS + bo + 2 * tq);
+      }
+    mma_chunk_pv<T>(qacc, da, w.K[buf], 0);
+    __syncwarp();
+  }
+  const T* bkp = a.blank_k ? (const T*)a.blank_k + (int64_t)h * TD : nullptr;
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int row = g + hf * 8;
+    if (row >= nq) continue;
+    const float dsb = bkp ? a.dsb[bh * N + n0 + row] : 0.f;
+    T* qrow = (T*)a.dq + (bh * N + n0 + row) * TD;
+#pragma unroll
+    for (int dt = 0; dt < 4; ++dt) {
+      const int col = dt * 8 + 2 * tq;
+      float v0 = qacc[dt][2 * hf], v1 = qacc[dt][2 * hf + 1];
+      if (bkp) { v0 += dsb * ldf(bkp + col); v1 += dsb * ldf(bkp + col + 1); }
+      *reinterpret_cast<uint32_t*>(qrow + col) = pack2<T>(v0 * a.scale, v1 * a.scale);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS) nbhd_blk_dq_kernel(NbhdArgs a) {
+  if (*a.general) return;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BlkDqSmem<T>& s = *reinterpret_cast<BlkDqSmem<T>*>(smem_raw);
+  const int N = a.N;
+  const int tiles = (N + TQ - 1) / TQ;
+  const int b = blockIdx.x / tiles;
+  const int n0 = (blockIdx.x % tiles) * TQ;
+  const int nq = min(TQ, N - n0);
+  const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
+  if (nclu < 0) return;  // excluded by the list check that cleared the flag
+  const int warp = threadIdx.x >> 5;
+  for (int h = warp; h < a.H; h += NW) blk_dq_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
 }
 
 template <typename K>
@@ -505,6 +602,11 @@ int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
 int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
   if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_bwd_kernel<__nv_bfloat16>, sizeof(BlkBwdSmem<__nv_bfloat16>), a, B, st);
   return launch_blk(nbhd_blk_bwd_kernel<__half>, sizeof(BlkBwdSmem<__half>), a, B, st);
+}
+
+int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
+  if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_dq_kernel<__nv_bfloat16>, sizeof(BlkDqSmem<__nv_bfloat16>), a, B, st);
+  return launch_blk(nbhd_blk_dq_kernel<__half>, sizeof(BlkDqSmem<__half>), a, B, st);
 }
 
 }  // namespace affb

@@ -149,6 +149,95 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
   }
 }
 
+// ------------------------------------------------------ query prologue --
+
+// Per (b, h, n): D = rowsum(O * dO) and, with a blank token, its probability
+// pb = exp(q . blank_k * scale - lse), dS_blank = pb (dO . blank_v - D), and
+// the blank gradients dblank_k += dS_blank q scale, dblank_v += pb dO
+// (reference local_attn.py:526-550).  One block per 64 rows of one (b, h),
+// four lanes per row, eight dims per lane.
+template <typename T>
+__global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs k) {
+  __shared__ float s_dbk[TD], s_dbv[TD];
+  if (*k.flag) return;
+  const int N = a.N;
+  const int nblk = (N + 63) / 64;
+  const int64_t bh = blockIdx.x / nblk;
+  const int h = (int)(bh % a.H);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, sub = lane & 3;
+  const int n = (blockIdx.x % nblk) * 64 + warp * 8 + (lane >> 2);
+  const bool valid = n < N;
+  const int64_t row = bh * N + n;
+  float ov[8], dv[8], di = 0.f;
+  if (valid) {
+    ld8((const T*)a.o + row * TD + sub * 8, ov);
+    ld8((const T*)a.dout + row * TD + sub * 8, dv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dv[e] = 0.f;
+  }
+  di += __shfl_xor_sync(0xffffffffu, di, 1);
+  di += __shfl_xor_sync(0xffffffffu, di, 2);
+  if (valid && sub == 0) k.di[row] = di;
+  if (!a.blank_k) return;
+  if (t < TD) { s_dbk[t] = 0.f; s_dbv[t] = 0.f; }
+  float qv[8], sb = 0.f, dpb = 0.f;
+  if (valid) {
+    float bkv[8], bvv[8];
+    ld8((const T*)a.q + row * TD + sub * 8, qv);
+    ld8((const T*)a.blank_k + (int64_t)h * TD + sub * 8, bkv);
+    ld8((const T*)a.blank_v + (int64_t)h * TD + sub * 8, bvv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qv[e] = 0.f;
+  }
+#pragma unroll
+  for (int o = 1; o < 4; o <<= 1) {
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
+  }
+  const float pb = valid ? expf(sb * a.scale - a.lse[row]) : 0.f;
+  const float dsb = pb * (dpb - di);
+  if (valid && sub == 0) k.dsb[row] = dsb;
+  float gk[8], gv[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    gk[e] = dsb * qv[e];
+    gv[e] = pb * dv[e];
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      gk[e] += __shfl_xor_sync(0xffffffffu, gk[e], o);
+      gv[e] += __shfl_xor_sync(0xffffffffu, gv[e], o);
+    }
+  }
+  __syncthreads();
+  if (lane < 4) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      atomicAdd(&s_dbk[sub * 8 + e], gk[e]);
+      atomicAdd(&s_dbv[sub * 8 + e], gv[e]);
+    }
+  }
+  __syncthreads();
+  if (t < TD) {
+    red_add(a.dbk + (int64_t)h * TD + t, s_dbk[t] * a.scale);
+    red_add(a.dbv + (int64_t)h * TD + t, s_dbv[t]);
+  }
+}
+
+int nbhd_q_prologue(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st) {
+  const int64_t blocks = (int64_t)B * a.H * ((a.N + 63) / 64);
+  if (blocks == 0) return AFFB_OK;
+  AFFB_REQUIRE(blocks < (1ll << 31), "nbhd_attn_bwd: too many rows");
+  if (dtype == AFFB_BF16) nbhd_q_prologue_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(a, k);
+  else nbhd_q_prologue_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(a, k);
+  return AFFB_OK;
+}
+
 // ------------------------------------------------------ key-major pass --
 
 template <typename T>
@@ -266,6 +355,10 @@ __device__ void kv_head(const NbhdArgs& a, const KvArgs& k, KvWarp<T>& w, const 
         const float p1 = v1 ? __expf(s[2 * hf + 1] * a.scale + b1 - ls) : 0.f;
         pp[hf] = pack2<T>(p0, p1);
         pd[hf] = pack2<T>(p0 * (dp[2 * hf] - dd), p1 * (dp[2 * hf + 1] - dd));
+        if (row < nr) {  // dS in bias layout: run j of query q, columns 2tq, 2tq+1
+          const int e = L[ch * 16 + row];
+          *reinterpret_cast<uint32_t*>((T*)k.ds + (bh * N + (e >> 3)) * a.M + 8 * (e & 7) + 2 * tq) = pd[hf];
+        }
       }
       const uint32_t bp[2] = {movmatrix_t(pp[0]), movmatrix_t(pp[1])};
       const uint32_t bd[2] = {movmatrix_t(pd[0]), movmatrix_t(pd[1])};
@@ -306,7 +399,7 @@ __device__ void kv_head(const NbhdArgs& a, const KvArgs& k, KvWarp<T>& w, const 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(TC_THREADS) nbhd_kv_kernel(NbhdArgs a, KvArgs k) {
+__global__ void __launch_bounds__(TC_THREADS, AFFB_KV_MINB) nbhd_kv_kernel(NbhdArgs a, KvArgs k) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   KvSmem<T>& s = *reinterpret_cast<KvSmem<T>*>(smem_raw);
   const int N = a.N, Cc = k.Cc;

@@ -15,6 +15,17 @@ constexpr int TC_THREADS = 128;
 constexpr int KST = TD + 8;     // smem row stride (elements) of Q/K/V/dO tiles: 80 B
 constexpr int NW = TC_THREADS / 32;
 
+// Minimum resident blocks per SM requested from the register allocator.
+#ifndef AFFB_FWD_MINB
+#define AFFB_FWD_MINB 1
+#endif
+#ifndef AFFB_BWD_MINB
+#define AFFB_BWD_MINB 1
+#endif
+#ifndef AFFB_KV_MINB
+#define AFFB_KV_MINB 6  // 80 registers: 6 blocks of the key-side kernel per SM
+#endif
+
 template <typename T> struct MmaType;
 template <> struct MmaType<__nv_bfloat16> {
   static __device__ __forceinline__ void mma(float* c, const uint32_t* a, const uint32_t* b) {

@@ -70,10 +70,12 @@ struct NbhdArgs {
   void* dbias;
   float* dbk;
   float* dbv;
-  // cluster-block backward: list-form flag (nonzero: dK / dV are scatter-added
-  // into dk / dv by the query side) and D = rowsum(O * dO) per (b, h, n)
+  // cluster-block backward: list-form flag (nonzero: the query-side kernel
+  // does the whole backward, scatter-adding dK / dV into dk / dv), dS in bias
+  // layout [B,H,N,M] and the blank token's dS per (b, h, n)
   const int* general;
-  float* di;
+  const void* ds;
+  const float* dsb;
 };
 
 // Forward of one (b, h, n) row by one warp.

@@ -24,6 +24,8 @@ struct NbhdBwdLayout {
   int* erk;
   int* entries;
   float* di;
+  float* dsb;
+  void* ds;
   float* acc_k;
   float* acc_v;
   size_t zero_bytes;  // flag + counts, cleared at the start of every call
@@ -52,6 +54,8 @@ inline NbhdBwdLayout nbhd_bwd_layout(bool tc, bool acc_sums, int64_t B, int64_t 
     ly.erk = (int*)take((size_t)(B * N * J) * 4);
     ly.entries = (int*)take((size_t)(B * N * J) * 4);
     ly.di = (float*)take((size_t)(B * H * N) * 4);
+    ly.dsb = (float*)take((size_t)(B * H * N) * 4);
+    ly.ds = take((size_t)(B * H * N * M) * 2);  // 16-bit dS when the call has no dbias output
   }
   if (acc_sums) {
     ly.acc_k = (float*)take(acc);
@@ -61,13 +65,15 @@ inline NbhdBwdLayout nbhd_bwd_layout(bool tc, bool acc_sums, int64_t B, int64_t 
   return ly;
 }
 
-// Arguments of the key-major pass.
+// Arguments of the key-side kernels.
 struct KvArgs {
   const int* flag;
   const int* counts;
   const int* offs;
   const int* entries;
-  const float* di;
+  float* di;         // D = rowsum(O * dO) per (b, h, n)
+  float* dsb;        // blank token's dS per (b, h, n)
+  void* ds;          // dS in bias layout [B,H,N,M] (the dbias output when there is a bias)
   const float* acc_k;
   const float* acc_v;
   void* dk;
@@ -78,8 +84,10 @@ struct KvArgs {
 // Query side (nbhd_attn_blk.cu).
 int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
+int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 // Key side (nbhd_attn_kv.cu).
 int nbhd_inv_lists(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, int B, cudaStream_t st);
+int nbhd_q_prologue(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st);
 int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st);
 
 }  // namespace affb

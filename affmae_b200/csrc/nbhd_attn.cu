@@ -157,6 +157,7 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
   if (nbhd_tc_supported(dtype, D, M)) {
     // lists -> prologue (D, blank terms) -> [query side, only for lists that
     // are not all cluster runs] -> key side (dK, dV, dS) -> dQ from dS
+    AFFB_REQUIRE(N * M < (1ll << 31), "nbhd_attn_bwd: N * M must be below 2^31 on the tensor-core path");
     a.dk = ly.acc_k; a.dv = ly.acc_v;
     a.general = ly.flag;
     KvArgs kv{};

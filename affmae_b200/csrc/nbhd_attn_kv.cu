@@ -33,7 +33,7 @@
 
 namespace affb {
 
-constexpr int KV_LCAP = 512;  // lists up to this length are sorted in shared memory
+constexpr int KV_LCAP = 256;  // list segment held in shared memory; shorter lists are sorted
 
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
@@ -55,19 +55,22 @@ __global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, i
   const int b = (int)(t / N);
   const int J = M >> 3;
   const int4* row = reinterpret_cast<const int4*>(midx + t * M);
+  int4 x[8], y[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (j < J) { x[j] = __ldg(row + 2 * j); y[j] = __ldg(row + 2 * j + 1); }
   int cs[8];
   bool ok = true;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     cs[j] = -1;
     if (j < J) {
-      const int4 x = __ldg(row + 2 * j), y = __ldg(row + 2 * j + 1);
-      const int c0 = x.x;
-      ok = ok && c0 >= 0 && (c0 & 7) == 0 && c0 <= N - 8 && x.y == c0 + 1 && x.z == c0 + 2 &&
-           x.w == c0 + 3 && y.x == c0 + 4 && y.y == c0 + 5 && y.z == c0 + 6 && y.w == c0 + 7;
+      const int c0 = x[j].x;
+      ok &= (c0 >= 0) & ((c0 & 7) == 0) & (c0 <= N - 8) & (x[j].y == c0 + 1) & (x[j].z == c0 + 2) &
+            (x[j].w == c0 + 3) & (y[j].x == c0 + 4) & (y[j].y == c0 + 5) & (y[j].z == c0 + 6) & (y[j].w == c0 + 7);
       cs[j] = c0 >> 3;
 #pragma unroll
-      for (int jj = 0; jj < j; ++jj) ok = ok && cs[jj] != cs[j];
+      for (int jj = 0; jj < j; ++jj) ok &= cs[jj] != cs[j];
     }
   }
   if (!ok) {
@@ -154,60 +157,69 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
 // Per (b, h, n): D = rowsum(O * dO) and, with a blank token, its probability
 // pb = exp(q . blank_k * scale - lse), dS_blank = pb (dO . blank_v - D), and
 // the blank gradients dblank_k += dS_blank q scale, dblank_v += pb dO
-// (reference local_attn.py:526-550).  One block per 64 rows of one (b, h),
-// four lanes per row, eight dims per lane.
+// (reference local_attn.py:526-550).  One block per PRO_ROWS rows of one
+// (b, h); four lanes per row, eight dims per lane; the blank gradients are
+// summed in registers over the block's rows and reduced once.
+constexpr int PRO_ROWS = 256;
+
 template <typename T>
 __global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs k) {
   __shared__ float s_dbk[TD], s_dbv[TD];
   if (*k.flag) return;
   const int N = a.N;
-  const int nblk = (N + 63) / 64;
+  const int nblk = (N + PRO_ROWS - 1) / PRO_ROWS;
   const int64_t bh = blockIdx.x / nblk;
   const int h = (int)(bh % a.H);
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, sub = lane & 3;
-  const int n = (blockIdx.x % nblk) * 64 + warp * 8 + (lane >> 2);
-  const bool valid = n < N;
-  const int64_t row = bh * N + n;
-  float ov[8], dv[8], di = 0.f;
-  if (valid) {
-    ld8((const T*)a.o + row * TD + sub * 8, ov);
-    ld8((const T*)a.dout + row * TD + sub * 8, dv);
+  const int t = threadIdx.x, lane = t & 31, sub = lane & 3;
+  const int nbase = (blockIdx.x % nblk) * PRO_ROWS;
+  const bool blank = a.blank_k != nullptr;
+  float bkv[8], bvv[8], gk[8], gv[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) dv[e] = 0.f;
-  }
-  di += __shfl_xor_sync(0xffffffffu, di, 1);
-  di += __shfl_xor_sync(0xffffffffu, di, 2);
-  if (valid && sub == 0) k.di[row] = di;
-  if (!a.blank_k) return;
-  if (t < TD) { s_dbk[t] = 0.f; s_dbv[t] = 0.f; }
-  float qv[8], sb = 0.f, dpb = 0.f;
-  if (valid) {
-    float bkv[8], bvv[8];
-    ld8((const T*)a.q + row * TD + sub * 8, qv);
+  for (int e = 0; e < 8; ++e) { gk[e] = 0.f; gv[e] = 0.f; }
+  if (blank) {
     ld8((const T*)a.blank_k + (int64_t)h * TD + sub * 8, bkv);
     ld8((const T*)a.blank_v + (int64_t)h * TD + sub * 8, bvv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qv[e] = 0.f;
+    if (t < TD) { s_dbk[t] = 0.f; s_dbv[t] = 0.f; }
   }
+#pragma unroll 1
+  for (int r0 = 0; r0 < PRO_ROWS; r0 += 64) {
+    const int n = nbase + r0 + (t >> 2);
+    const bool valid = n < N;
+    const int64_t row = bh * N + n;
+    float ov[8], dv[8], qv[8], di = 0.f;
+    if (valid) {
+      ld8((const T*)a.o + row * TD + sub * 8, ov);
+      ld8((const T*)a.dout + row * TD + sub * 8, dv);
+      if (blank) ld8((const T*)a.q + row * TD + sub * 8, qv);
 #pragma unroll
-  for (int o = 1; o < 4; o <<= 1) {
-    sb += __shfl_xor_sync(0xffffffffu, sb, o);
-    dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
+      for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
+    }
+    di += __shfl_xor_sync(0xffffffffu, di, 1);
+    di += __shfl_xor_sync(0xffffffffu, di, 2);
+    if (valid && sub == 0) k.di[row] = di;
+    if (blank) {
+      float sb = 0.f, dpb = 0.f;
+      if (valid) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
+      }
+#pragma unroll
+      for (int o = 1; o < 4; o <<= 1) {
+        sb += __shfl_xor_sync(0xffffffffu, sb, o);
+        dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
+      }
+      if (valid) {
+        const float pb = expf(sb * a.scale - a.lse[row]);
+        const float dsb = pb * (dpb - di);
+        if (sub == 0) k.dsb[row] = dsb;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { gk[e] = fmaf(dsb, qv[e], gk[e]); gv[e] = fmaf(pb, dv[e], gv[e]); }
+      }
+    }
   }
-  const float pb = valid ? expf(sb * a.scale - a.lse[row]) : 0.f;
-  const float dsb = pb * (dpb - di);
-  if (valid && sub == 0) k.dsb[row] = dsb;
-  float gk[8], gv[8];
+  if (!blank) return;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    gk[e] = dsb * qv[e];
-    gv[e] = pb * dv[e];
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       gk[e] += __shfl_xor_sync(0xffffffffu, gk[e], o);
@@ -230,7 +242,7 @@ __global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs
 }
 
 int nbhd_q_prologue(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st) {
-  const int64_t blocks = (int64_t)B * a.H * ((a.N + 63) / 64);
+  const int64_t blocks = (int64_t)B * a.H * ((a.N + PRO_ROWS - 1) / PRO_ROWS);
   if (blocks == 0) return AFFB_OK;
   AFFB_REQUIRE(blocks < (1ll << 31), "nbhd_attn_bwd: too many rows");
   if (dtype == AFFB_BF16) nbhd_q_prologue_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(a, k);
@@ -252,165 +264,166 @@ struct KvWarp {
   alignas(16) float di[2][16];
   alignas(16) T ost[8 * KST];
 };
+// The block's list (or a segment of it) as per-entry offsets shared by the
+// heads: qoff = q * D (Q / dO rows), roff = q * M + 8 j (bias / mask / dS runs).
 template <typename T>
 struct KvSmem {
-  int list[KV_LCAP];
-  int tmp[KV_LCAP];
+  int qoff[KV_LCAP];
+  int roff[KV_LCAP];
   KvWarp<T> w[NW];
 };
+static_assert(sizeof(((KvWarp<__half>*)0)->Q) >= KV_LCAP * sizeof(int), "sort buffer aliases a Q stage");
 
-// Gathers chunk rows base .. base+15 of list L (n entries) into stage `buf`.
+// Per-head base pointers of the key-side kernel.
 template <typename T>
-__device__ __forceinline__ void kv_stage(const NbhdArgs& a, const KvArgs& k, KvWarp<T>& w, const int* L, int n,
-                                         int base, int buf, int b, int h) {
+struct KvHead {
+  const T* q;
+  const T* dout;
+  const T* bias;
+  const uint8_t* mask;
+  const float* lse;
+  const float* di;
+  T* ds;
+};
+
+// Gathers chunk rows base .. base+15 (of ns entries) into stage `buf`.
+template <typename T>
+__device__ __forceinline__ void kv_stage(const KvHead<T>& p, const KvSmem<T>& s, KvWarp<T>& w, int ns, int base,
+                                         int buf) {
   const int lane = threadIdx.x & 31;
-  const int N = a.N, M = a.M;
-  const int64_t bh = (int64_t)b * a.H + h;
-  const int nr = n - base;
+  const int nr = ns - base;
 #pragma unroll
   for (int i = lane; i < 64; i += 32) {
     const int row = i >> 2, piece = i & 3;
     const bool valid = row < nr;
-    const int q = valid ? (L[base + row] >> 3) : 0;
-    cp_async16(w.Q[buf] + row * KST + piece * 8, (const T*)a.q + (bh * N + q) * TD + piece * 8, valid);
-    cp_async16(w.dO[buf] + row * KST + piece * 8, (const T*)a.dout + (bh * N + q) * TD + piece * 8, valid);
+    const int qo = (valid ? s.qoff[base + row] : 0) + piece * 8;
+    cp_async16(w.Q[buf] + row * KST + piece * 8, p.q + qo, valid);
+    cp_async16(w.dO[buf] + row * KST + piece * 8, p.dout + qo, valid);
   }
   const int row = lane & 15;
   const bool valid = row < nr;
-  const int e = valid ? L[base + row] : 0;
-  const int q = e >> 3, j = e & 7;
+  const int q = valid ? s.qoff[base + row] / TD : 0;
+  const int ro = valid ? s.roff[base + row] : 0;
   if (lane < 16) {
-    if (a.bias) cp_async16(w.bias[buf] + row * 8, (const T*)a.bias + (bh * N + q) * M + 8 * j, valid);
-    cp_async4(&w.lse[buf][row], a.lse + bh * N + q, valid);
+    if (p.bias) cp_async16(w.bias[buf] + row * 8, p.bias + ro, valid);
+    cp_async4(&w.lse[buf][row], p.lse + q, valid);
   } else {
-    if (a.mask) {
-      const int64_t mh = a.mask_heads == 1 ? 0 : h;
-      cp_async8(w.mask[buf] + row * 8, a.mask + (((int64_t)b * a.mask_heads + mh) * N + q) * M + 8 * j, valid);
-    }
-    cp_async4(&w.di[buf][row], k.di + bh * N + q, valid);
+    if (p.mask) cp_async8(w.mask[buf] + row * 8, p.mask + ro, valid);
+    cp_async4(&w.di[buf][row], p.di + q, valid);
   }
 }
 
+// Chunks of one list segment (ns entries in s) for one head: accumulates
+// dK^T, dV^T and writes dS.
 template <typename T>
-__device__ void kv_head(const NbhdArgs& a, const KvArgs& k, KvWarp<T>& w, const int* L, int n, int b, int h,
-                        int c) {
+__device__ __forceinline__ void kv_segment(const NbhdArgs& a, const KvHead<T>& p, const KvSmem<T>& s, KvWarp<T>& w,
+                                           int ns, uint32_t* bk, uint32_t* bv, bool& frags, float (*dkt)[4],
+                                           float (*dvt)[4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
-  const int N = a.N;
-  const int64_t bh = (int64_t)b * a.H + h;
-  const int kr0 = 8 * c, nkeys = min(8, N - kr0);
-  float dkt[2][4], dvt[2][4];
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) dkt[i][e] = dvt[i][e] = 0.f;
-  if (n > 0) {
-    {
-      const int row = lane >> 2, piece = lane & 3;
-      const bool valid = row < nkeys;
-      const int64_t src = (bh * N + kr0 + (valid ? row : 0)) * TD + piece * 8;
-      cp_async16(w.K + row * KST + piece * 8, (const T*)a.k + src, valid);
-      cp_async16(w.V + row * KST + piece * 8, (const T*)a.v + src, valid);
-    }
-    kv_stage<T>(a, k, w, L, n, 0, 0, b, h);
+  const int nch = (ns + 15) >> 4;
+  kv_stage<T>(p, s, w, ns, 0, 0);
+  cp_commit();
+  for (int ch = 0; ch < nch; ++ch) {
+    const int buf = ch & 1;
+    if (ch + 1 < nch) kv_stage<T>(p, s, w, ns, (ch + 1) * 16, buf ^ 1);
     cp_commit();
-    const int nch = (n + 15) >> 4;
-    uint32_t bk[4], bv[4];
-    for (int ch = 0; ch < nch; ++ch) {
-      const int buf = ch & 1;
-      if (ch + 1 < nch) kv_stage<T>(a, k, w, L, n, (ch + 1) * 16, buf ^ 1, b, h);
-      cp_commit();
-      cp_wait<1>();
-      __syncwarp();
-      if (ch == 0) {
-        ldsm_x4(bk, w.K + (lane & 7) * KST + (lane >> 3) * 8);
-        ldsm_x4(bv, w.V + (lane & 7) * KST + (lane >> 3) * 8);
-      }
-      uint32_t aq[2][4], ado[2][4];
-      load_a_frags(aq, w.Q[buf]);
-      load_a_frags(ado, w.dO[buf]);
-      float s[4] = {0.f, 0.f, 0.f, 0.f}, dp[4] = {0.f, 0.f, 0.f, 0.f};
-      MmaType<T>::mma(s, aq[0], bk);
-      MmaType<T>::mma(s, aq[1], bk + 2);
-      MmaType<T>::mma(dp, ado[0], bv);
-      MmaType<T>::mma(dp, ado[1], bv + 2);
-      const int nr = n - ch * 16;
-      uint32_t pp[2], pd[2];
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int row = g + 8 * hf;
-        const float ls = w.lse[buf][row], dd = w.di[buf][row];
-        float b0 = 0.f, b1 = 0.f;
-        if (a.bias) {
-          const uint32_t u = *reinterpret_cast<const uint32_t*>(w.bias[buf] + row * 8 + 2 * tq);
-          const T* hp = reinterpret_cast<const T*>(&u);
-          b0 = io<T>::ld(hp);
-          b1 = io<T>::ld(hp + 1);
-        }
-        bool v0 = row < nr, v1 = v0;
-        if (a.mask) {
-          v0 = v0 && w.mask[buf][row * 8 + 2 * tq] != 0;
-          v1 = v1 && w.mask[buf][row * 8 + 2 * tq + 1] != 0;
-        }
-        const float p0 = v0 ? __expf(s[2 * hf] * a.scale + b0 - ls) : 0.f;
-        const float p1 = v1 ? __expf(s[2 * hf + 1] * a.scale + b1 - ls) : 0.f;
-        pp[hf] = pack2<T>(p0, p1);
-        pd[hf] = pack2<T>(p0 * (dp[2 * hf] - dd), p1 * (dp[2 * hf + 1] - dd));
-        if (row < nr) {  // dS in bias layout: run j of query q, columns 2tq, 2tq+1
-          const int e = L[ch * 16 + row];
-          *reinterpret_cast<uint32_t*>((T*)k.ds + (bh * N + (e >> 3)) * a.M + 8 * (e & 7) + 2 * tq) = pd[hf];
-        }
-      }
-      const uint32_t bp[2] = {movmatrix_t(pp[0]), movmatrix_t(pp[1])};
-      const uint32_t bd[2] = {movmatrix_t(pd[0]), movmatrix_t(pd[1])};
-      const int mi = lane >> 3;
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        // A[m = dim][k = query] = X[query][dim]: matrices (d 0-7, q 0-7), (d 8-15, q 0-7), (d 0-7, q 8-15), (d 8-15, q 8-15)
-        const int off = ((mi >> 1) * 8 + (lane & 7)) * KST + (mt * 2 + (mi & 1)) * 8;
-        uint32_t ad[4], aqt[4];
-        ldsm_x4_t(ad, w.dO[buf] + off);
-        ldsm_x4_t(aqt, w.Q[buf] + off);
-        MmaType<T>::mma(dvt[mt], ad, bp);
-        MmaType<T>::mma(dkt[mt], aqt, bd);
-      }
-      __syncwarp();
-    }
-  }
-  // transpose through shared memory and store 16-byte pieces of the key rows
-#pragma unroll
-  for (int pass = 0; pass < 2; ++pass) {
-    const float(*acc)[4] = pass == 0 ? dkt : dvt;
-    const float mul = pass == 0 ? a.scale : 1.f;
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = mt * 16 + g + (e >> 1) * 8, key = 2 * tq + (e & 1);
-        io<T>::st(w.ost + key * KST + d, acc[mt][e] * mul);
-      }
+    cp_wait<1>();
     __syncwarp();
-    const int row = lane >> 2, piece = lane & 3;
-    if (row < nkeys) {
-      T* dst = (T*)(pass == 0 ? k.dk : k.dv) + (bh * N + kr0 + row) * TD + piece * 8;
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(w.ost + row * KST + piece * 8);
+    if (!frags) {  // K / V rows of the cluster arrived with the first stage
+      ldsm_x4(bk, w.K + (lane & 7) * KST + (lane >> 3) * 8);
+      ldsm_x4(bv, w.V + (lane & 7) * KST + (lane >> 3) * 8);
+      frags = true;
+    }
+    uint32_t aq[2][4], ado[2][4];
+    load_a_frags(aq, w.Q[buf]);
+    load_a_frags(ado, w.dO[buf]);
+    float sc[4] = {0.f, 0.f, 0.f, 0.f}, dp[4] = {0.f, 0.f, 0.f, 0.f};
+    MmaType<T>::mma(sc, aq[0], bk);
+    MmaType<T>::mma(sc, aq[1], bk + 2);
+    MmaType<T>::mma(dp, ado[0], bv);
+    MmaType<T>::mma(dp, ado[1], bv + 2);
+    const int nr = ns - ch * 16;
+    uint32_t pp[2], pd[2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = g + 8 * hf;
+      const float ls = w.lse[buf][row], dd = w.di[buf][row];
+      float b0 = 0.f, b1 = 0.f;
+      if (p.bias) {
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(w.bias[buf] + row * 8 + 2 * tq);
+        const T* hp = reinterpret_cast<const T*>(&u);
+        b0 = io<T>::ld(hp);
+        b1 = io<T>::ld(hp + 1);
+      }
+      bool v0 = row < nr, v1 = v0;
+      if (p.mask) {
+        v0 = v0 && w.mask[buf][row * 8 + 2 * tq] != 0;
+        v1 = v1 && w.mask[buf][row * 8 + 2 * tq + 1] != 0;
+      }
+      const float p0 = v0 ? __expf(sc[2 * hf] * a.scale + b0 - ls) : 0.f;
+      const float p1 = v1 ? __expf(sc[2 * hf + 1] * a.scale + b1 - ls) : 0.f;
+      pp[hf] = pack2<T>(p0, p1);
+      pd[hf] = pack2<T>(p0 * (dp[2 * hf] - dd), p1 * (dp[2 * hf + 1] - dd));
+      // dS in bias layout: run j of query q, columns 2tq, 2tq+1
+      if (row < nr) *reinterpret_cast<uint32_t*>(p.ds + s.roff[ch * 16 + row] + 2 * tq) = pd[hf];
+    }
+    const uint32_t bp[2] = {movmatrix_t(pp[0]), movmatrix_t(pp[1])};
+    const uint32_t bd[2] = {movmatrix_t(pd[0]), movmatrix_t(pd[1])};
+    const int mi = lane >> 3;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      // A[m = dim][k = query] = X[query][dim]: matrices (d 0-7, q 0-7), (d 8-15, q 0-7), (d 0-7, q 8-15), (d 8-15, q 8-15)
+      const int off = ((mi >> 1) * 8 + (lane & 7)) * KST + (mt * 2 + (mi & 1)) * 8;
+      uint32_t ad[4], aqt[4];
+      ldsm_x4_t(ad, w.dO[buf] + off);
+      ldsm_x4_t(aqt, w.Q[buf] + off);
+      MmaType<T>::mma(dvt[mt], ad, bp);
+      MmaType<T>::mma(dkt[mt], aqt, bd);
     }
     __syncwarp();
   }
+}
+
+// Loads entries [seg0, seg0 + ns) of the list into the offset tables, sorted
+// by query when `sort` (the whole list is one segment).
+template <typename T>
+__device__ __forceinline__ void kv_load_segment(KvSmem<T>& s, const int* src, int ns, int M, bool sort) {
+  const int t = threadIdx.x;
+  __syncthreads();  // previous segment no longer read
+  if (!sort) {
+    for (int i = t; i < ns; i += TC_THREADS) {
+      const int e = src[i];
+      s.qoff[i] = (e >> 3) * TD;
+      s.roff[i] = (e >> 3) * M + 8 * (e & 7);
+    }
+  } else {  // rank sort (entries are distinct); before any staging, so a Q stage holds the copy
+    int* tmp = reinterpret_cast<int*>(s.w[0].Q);
+    for (int i = t; i < ns; i += TC_THREADS) tmp[i] = src[i];
+    __syncthreads();
+    for (int i = t; i < ns; i += TC_THREADS) {
+      const int e = tmp[i];
+      int r = 0;
+      for (int m = 0; m < ns; ++m) r += tmp[m] < e;
+      s.qoff[r] = (e >> 3) * TD;
+      s.roff[r] = (e >> 3) * M + 8 * (e & 7);
+    }
+  }
+  __syncthreads();
 }
 
 template <typename T>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_KV_MINB) nbhd_kv_kernel(NbhdArgs a, KvArgs k) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   KvSmem<T>& s = *reinterpret_cast<KvSmem<T>*>(smem_raw);
-  const int N = a.N, Cc = k.Cc;
+  const int N = a.N, M = a.M, Cc = k.Cc;
   const int b = blockIdx.x / Cc, c = blockIdx.x % Cc;
-  const int t = threadIdx.x, warp = t >> 5;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, g = lane >> 2, tq = lane & 3;
+  const int kr0 = 8 * c, nkeys = min(8, N - kr0);
   if (*k.flag) {  // general lists: convert the fp32 sums of the query side
-    const int nkeys = min(8, N - 8 * c);
     const int per_head = nkeys * TD;
     for (int i = t; i < a.H * per_head; i += TC_THREADS) {
       const int h = i / per_head, r = i % per_head;
-      const int64_t o = (((int64_t)b * a.H + h) * N + 8 * c) * TD + r;
+      const int64_t o = (((int64_t)b * a.H + h) * N + kr0) * TD + r;
       io<T>::st((T*)k.dk + o, k.acc_k[o]);
       io<T>::st((T*)k.dv + o, k.acc_v[o]);
     }
@@ -419,20 +432,62 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_KV_MINB) nbhd_kv_kernel(NbhdA
   const int64_t cell = (int64_t)b * Cc + c;
   const int n = k.counts[cell];
   const int* src = k.entries + k.offs[cell];
-  const int* L = src;
-  if (n <= KV_LCAP) {  // rank sort by query (entries are distinct)
-    for (int i = t; i < n; i += TC_THREADS) s.tmp[i] = src[i];
-    __syncthreads();
-    for (int i = t; i < n; i += TC_THREADS) {
-      const int e = s.tmp[i];
-      int r = 0;
-      for (int m = 0; m < n; ++m) r += s.tmp[m] < e;
-      s.list[r] = e;
+  const bool one = n <= KV_LCAP;
+  if (one) kv_load_segment(s, src, n, M, true);
+  KvWarp<T>& w = s.w[warp];
+  for (int hg = 0; hg < a.H; hg += NW) {
+    const int h = hg + warp;
+    const bool act = h < a.H;
+    const int64_t bh = (int64_t)b * a.H + h;
+    KvHead<T> p;
+    p.q = (const T*)a.q + bh * N * TD;
+    p.dout = (const T*)a.dout + bh * N * TD;
+    p.bias = a.bias ? (const T*)a.bias + bh * N * M : nullptr;
+    p.mask = a.mask ? a.mask + ((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N * M : nullptr;
+    p.lse = a.lse + bh * N;
+    p.di = k.di + bh * N;
+    p.ds = (T*)k.ds + bh * N * M;
+    float dkt[2][4], dvt[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dkt[i][e] = dvt[i][e] = 0.f;
+    uint32_t bk[4], bv[4];
+    bool frags = false;
+    if (act && n > 0) {  // completes with the first stage of kv_segment
+      const int row = lane >> 2, piece = lane & 3;
+      const bool valid = row < nkeys;
+      const int64_t off = (bh * N + kr0 + (valid ? row : 0)) * TD + piece * 8;
+      cp_async16(w.K + row * KST + piece * 8, (const T*)a.k + off, valid);
+      cp_async16(w.V + row * KST + piece * 8, (const T*)a.v + off, valid);
     }
-    __syncthreads();
-    L = s.list;
+    for (int seg0 = 0; seg0 < n; seg0 += KV_LCAP) {
+      const int ns = min(KV_LCAP, n - seg0);
+      if (!one) kv_load_segment(s, src + seg0, ns, M, false);
+      if (act) kv_segment<T>(a, p, s, w, ns, bk, bv, frags, dkt, dvt);
+    }
+    if (!act) continue;
+    // transpose through shared memory and store 16-byte pieces of the key rows
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const float(*acc)[4] = pass == 0 ? dkt : dvt;
+      const float mul = pass == 0 ? a.scale : 1.f;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = mt * 16 + g + (e >> 1) * 8, key = 2 * tq + (e & 1);
+          io<T>::st(w.ost + key * KST + d, acc[mt][e] * mul);
+        }
+      __syncwarp();
+      const int row = lane >> 2, piece = lane & 3;
+      if (row < nkeys) {
+        T* dst = (T*)(pass == 0 ? k.dk : k.dv) + (bh * N + kr0 + row) * TD + piece * 8;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(w.ost + row * KST + piece * 8);
+      }
+      __syncwarp();
+    }
   }
-  for (int h = warp; h < a.H; h += NW) kv_head<T>(a, k, s.w[warp], L, n, b, h, c);
 }
 
 int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st) {

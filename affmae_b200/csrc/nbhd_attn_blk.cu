@@ -30,62 +30,64 @@
 
 namespace affb {
 
-constexpr int UCLU = TQ * MMAX / 8;  // clusters per tile: every row's list, all distinct
 constexpr int CHS = 256;         // cluster hash slots
 constexpr int BPT = 24;          // 16-bit row stride of the per-warp 16x16 P / dS tiles
-constexpr int BSENT = TQ * MMAX; // offset of the -inf block that ends each staged bias tile
 
+// Tile structures for lists of at most MM neighbours (the call's M rounded up
+// to 16, 32, 48 or 64), so that shared memory follows M.  The staged bias /
+// dS tile of a warp is [16][M] (row stride M) followed, at offset 16 MM, by an
+// 8-element block that absent clusters point at (-inf for bias, zeros for dS).
+template <int MM>
 struct BlkSetup {
-  alignas(16) int idx[TQ * MMAX];  // staged neighbour rows
-  int uclu[UCLU];                  // cluster ids of the union (key rows 8c .. 8c+7)
-  int16_t boff[TQ][UCLU];          // row q, cluster slot u: offset q*M + 8j of its bias run in the
-                                   // staged tile (list position j), BSENT when q does not list it
+  static constexpr int UCL = TQ * MM / 8;  // clusters per tile: every row's list, all distinct
+  int uclu[UCL];                   // cluster ids of the union (key rows 8c .. 8c+7)
+  int16_t boff[TQ][UCL];           // row q, cluster slot u: offset q*M + 8j of its bias run in the
+                                   // staged tile (list position j), 16 MM when q does not list it
   int hkey[CHS], hval[CHS];
   int warp_tot[NW];
-  int nclu, fail;
+  int fail;
 };
 
-template <typename T>
+template <typename T, int MM>
 struct BlkWarpFwd {
-  alignas(16) T Q[TQ * KST];
-  alignas(16) T bias[TQ * MMAX + 8];
-  alignas(16) T KV[2][2][16 * KST];
+  alignas(16) T Q[TQ * TD];
+  alignas(16) T bias[TQ * MM + 8];
+  alignas(16) T KV[2][2][16 * TD];
 };
-template <typename T>
+template <typename T, int MM>
 struct BlkWarpBwd {
-  alignas(16) T Q[TQ * KST];
-  alignas(16) T dO[TQ * KST];
-  alignas(16) T bias[TQ * MMAX + 8];
-  alignas(16) T KV[2][2][16 * KST];
+  alignas(16) T Q[TQ * TD];
+  alignas(16) T dO[TQ * TD];
+  alignas(16) T bias[TQ * MM + 8];
+  alignas(16) T KV[2][2][16 * TD];
   alignas(16) T P[TQ * BPT];
   alignas(16) T dS[TQ * BPT];
 };
-template <typename T>
+template <typename T, int MM>
 struct BlkWarpDq {
-  alignas(16) T dS[TQ * MMAX + 8];
-  alignas(16) T K[2][16 * KST];
+  alignas(16) T dS[TQ * MM + 8];
+  alignas(16) T K[2][16 * TD];
 };
-template <typename T>
-struct BlkFwdSmem {
-  BlkSetup setup;
-  BlkWarpFwd<T> w[NW];
+// The staged neighbour rows are read only by the setup, before any warp
+// buffer is written, so they share storage with the warps' buffers.
+template <int MM, typename W>
+struct BlkSmem {
+  BlkSetup<MM> setup;
+  union U {
+    int idx[TQ * MM];
+    W w[NW];
+  } u;
 };
-template <typename T>
-struct BlkBwdSmem {
-  BlkSetup setup;
-  BlkWarpBwd<T> w[NW];
-};
-template <typename T>
-struct BlkDqSmem {
-  BlkSetup setup;
-  BlkWarpDq<T> w[NW];
-};
+template <typename T, int MM> using BlkFwdSmem = BlkSmem<MM, BlkWarpFwd<T, MM>>;
+template <typename T, int MM> using BlkBwdSmem = BlkSmem<MM, BlkWarpBwd<T, MM>>;
+template <typename T, int MM> using BlkDqSmem = BlkSmem<MM, BlkWarpDq<T, MM>>;
 
 __device__ __forceinline__ uint32_t clu_slot(int key) { return ((uint32_t)key * 2654435761u) >> 24; }
 
 // Checks the cluster-block form of the tile and builds its cluster union.
 // Returns the number of clusters, or -1 when the tile needs the general path.
-__device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, int n0, int nq, int N, int M) {
+template <int MM>
+__device__ int blk_setup(BlkSetup<MM>& s, int* sidx, const int32_t* __restrict__ midx, int b, int n0, int nq, int N, int M) {
   const int t = threadIdx.x;
   const int J = M >> 3;  // clusters per list
   {
@@ -93,13 +95,13 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
     const int nch = TQ * M / 4;  // 16-byte chunks of int32
     for (int i = t; i < nch; i += TC_THREADS) {
       const bool ok = (i * 4) / M < nq;
-      cp_async16(s.idx + i * 4, src + (ok ? i * 4 : 0), ok);
+      cp_async16(sidx + i * 4, src + (ok ? i * 4 : 0), ok);
     }
     cp_commit();
   }
   for (int i = t; i < CHS; i += TC_THREADS) s.hkey[i] = -1;
-  for (int i = t; i < TQ * UCLU / 2; i += TC_THREADS)
-    reinterpret_cast<int*>(&s.boff[0][0])[i] = BSENT | (BSENT << 16);
+  for (int i = t; i < TQ * BlkSetup<MM>::UCL / 2; i += TC_THREADS)
+    reinterpret_cast<int*>(&s.boff[0][0])[i] = (TQ * MM) | ((TQ * MM) << 16);
   if (t == 0) s.fail = 0;
   cp_wait<0>();
   __syncthreads();
@@ -107,12 +109,12 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
   int cid = -1;
   const int q = t / 8, j = t % 8;  // TQ * 8 = 128 items cover J <= 8
   if (q < nq && j < J) {
-    const int* run = s.idx + q * M + 8 * j;
+    const int* run = sidx + q * M + 8 * j;
     const int c0 = run[0];
     bool ok = c0 >= 0 && (c0 & 7) == 0 && c0 + 8 <= N;
 #pragma unroll
     for (int r = 1; r < 8; ++r) ok = ok && run[r] == c0 + r;
-    for (int jj = 0; jj < j; ++jj) ok = ok && s.idx[q * M + 8 * jj] != c0;  // listed twice in one row
+    for (int jj = 0; jj < j; ++jj) ok = ok && sidx[q * M + 8 * jj] != c0;  // listed twice in one row
     if (ok) {
       cid = c0 >> 3;
       uint32_t h = clu_slot(cid);
@@ -165,9 +167,9 @@ __device__ int blk_setup(BlkSetup& s, const int32_t* __restrict__ midx, int b, i
 }
 
 // Staged bias tile of one warp: rows [16][M] of bias (zeros without bias),
-// -inf where the mask is 0, and the -inf block at BSENT for absent clusters.
+// -inf where the mask is 0, and the -inf block at offset 16 MM for absent clusters.
 // Called once the bias cp.async group has completed.
-template <typename T>
+template <typename T, int MM>
 __device__ __forceinline__ void warp_finish_bias(T* sb, const NbhdArgs& a, const uint8_t* mrow, int nq) {
   const int lane = threadIdx.x & 31, M = a.M;
   const T ninf = neg_inf<T>();
@@ -178,7 +180,7 @@ __device__ __forceinline__ void warp_finish_bias(T* sb, const NbhdArgs& a, const
   if (mrow)
     for (int i = lane; i < nq * M; i += 32)
       if (mrow[i] == 0) sb[i] = ninf;
-  if (lane < 8) sb[BSENT + lane] = ninf;
+  if (lane < 8) sb[TQ * MM + lane] = ninf;
   __syncwarp();
 }
 
@@ -201,7 +203,7 @@ __device__ __forceinline__ void warp_load_k(T* dk, const T* __restrict__ kb, con
     const int u = 2 * c + hh;
     const bool ok = u < nclu;
     const int64_t src = (int64_t)(ok ? uclu[u] * 8 + r : 0) * TD + piece * 8;
-    cp_async16(dk + (hh * 8 + r) * KST + piece * 8, kb + src, ok);
+    cp_async16(dk + swz(hh * 8 + r, piece), kb + src, ok);
   }
 }
 
@@ -216,14 +218,14 @@ __device__ __forceinline__ void warp_load_kv(T* dk, T* dv, const T* __restrict__
     const int u = 2 * c + hh;
     const bool ok = u < nclu;
     const int64_t src = (int64_t)(ok ? uclu[u] * 8 + r : 0) * TD + piece * 8;
-    const int dst = (hh * 8 + r) * KST + piece * 8;
+    const int dst = swz(hh * 8 + r, piece);
     cp_async16(dk + dst, kb + src, ok);
     cp_async16(dv + dst, vb + src, ok);
   }
 }
 
-template <typename T>
-__device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>& w, int b, int h, int n0,
+template <typename T, int MM>
+__device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpFwd<T, MM>& w, int b, int h, int n0,
                              int nq, int nclu) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int N = a.N, M = a.M;
@@ -253,7 +255,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
   }
   cp_wait<1>();
   __syncwarp();
-  warp_finish_bias(w.bias, a, mrow, nq);
+  warp_finish_bias<T, MM>(w.bias, a, mrow, nq);
   uint32_t aq[2][4];
   load_a_frags(aq, w.Q);
   float sbv[2] = {-INFINITY, -INFINITY};
@@ -339,29 +341,29 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpFwd<T>
   }
 }
 
-template <typename T>
+template <typename T, int MM>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_FWD_MINB) nbhd_blk_fwd_kernel(NbhdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  BlkFwdSmem<T>& s = *reinterpret_cast<BlkFwdSmem<T>*>(smem_raw);
+  BlkFwdSmem<T, MM>& s = *reinterpret_cast<BlkFwdSmem<T, MM>*>(smem_raw);
   const int N = a.N;
   const int tiles = (N + TQ - 1) / TQ;
   const int b = blockIdx.x / tiles;
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
+  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
   const int warp = threadIdx.x >> 5;
   if (nclu < 0) {  // not cluster-block lists: CUDA-core rows
     for (int w = warp; w < a.H * nq; w += NW) nbhd_fwd_row<T, 4>(a, b, w / nq, n0 + w % nq);
     return;
   }
-  for (int h = warp; h < a.H; h += NW) blk_fwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  for (int h = warp; h < a.H; h += NW) blk_fwd_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);
 }
 
 // Full backward of one head for calls whose lists are not all cluster runs:
 // dQ, dbias and the blank-token gradients, with dK / dV scatter-added into
 // the fp32 sums a.dk / a.dv.
-template <typename T>
-__device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>& w, int b, int h, int n0,
+template <typename T, int MM>
+__device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpBwd<T, MM>& w, int b, int h, int n0,
                              int nq, int nclu) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int N = a.N, M = a.M;
@@ -398,7 +400,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
   }
   cp_wait<1>();
   __syncwarp();
-  warp_finish_bias(w.bias, a, mrow, nq);
+  warp_finish_bias<T, MM>(w.bias, a, mrow, nq);
   uint32_t aq[2][4], ado[2][4];
   load_a_frags(aq, w.Q);
   load_a_frags(ado, w.dO);
@@ -418,8 +420,8 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
       const int src = (row & 7) * 4;
       const float ds_r = __shfl_sync(0xffffffffu, row < 8 ? dsb[0] : dsb[1], src);
       const float pb_r = __shfl_sync(0xffffffffu, row < 8 ? pbv[0] : pbv[1], src);
-      gk = fmaf(ds_r, io<T>::ld(w.Q + row * KST + lane), gk);
-      gv = fmaf(pb_r, io<T>::ld(w.dO + row * KST + lane), gv);
+      gk = fmaf(ds_r, io<T>::ld(w.Q + swz(row, lane >> 3) + (lane & 7)), gk);
+      gv = fmaf(pb_r, io<T>::ld(w.dO + swz(row, lane >> 3) + (lane & 7)), gv);
     }
     red_add(a.dbk + (int64_t)h * TD + lane, gk * a.scale);
     red_add(a.dbv + (int64_t)h * TD + lane, gv);
@@ -452,7 +454,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
         ds[nt][2 * hf] = p[nt][2 * hf] * (dp[nt][2 * hf] - dl[hf]);
         ds[nt][2 * hf + 1] = p[nt][2 * hf + 1] * (dp[nt][2 * hf + 1] - dl[hf]);
         const uint32_t dpk = pack2<T>(ds[nt][2 * hf], ds[nt][2 * hf + 1]);
-        if (dbase && bo != BSENT && row < nq) *reinterpret_cast<uint32_t*>(dbase + bo + 2 * tq) = dpk;
+        if (dbase && bo != TQ * MM && row < nq) *reinterpret_cast<uint32_t*>(dbase + bo + 2 * tq) = dpk;
         *reinterpret_cast<uint32_t*>(w.dS + row * BPT + lc) = dpk;
         *reinterpret_cast<uint32_t*>(w.P + row * BPT + lc) = pack2<T>(p[nt][2 * hf], p[nt][2 * hf + 1]);
       }
@@ -483,17 +485,17 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpBwd<T>
 
 // Only for calls whose lists are not all cluster runs (flag set by the list
 // builder); otherwise the key-side and dQ kernels do the backward.
-template <typename T>
+template <typename T, int MM>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel(NbhdArgs a) {
   if (!*a.general) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  BlkBwdSmem<T>& s = *reinterpret_cast<BlkBwdSmem<T>*>(smem_raw);
+  BlkBwdSmem<T, MM>& s = *reinterpret_cast<BlkBwdSmem<T, MM>*>(smem_raw);
   const int N = a.N;
   const int tiles = (N + TQ - 1) / TQ;
   const int b = blockIdx.x / tiles;
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
+  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
   const int warp = threadIdx.x >> 5;
   if (nclu < 0) {  // not cluster-block lists: CUDA-core rows, blank-token grads straight to global
     for (int w = warp; w < a.H * nq; w += NW) {
@@ -502,7 +504,7 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel
     }
     return;
   }
-  for (int h = warp; h < a.H; h += NW) blk_bwd_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);
 }
 
 // dQ of one head and tile from dS, which the key-side kernel has written in
@@ -510,8 +512,8 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel
 // ds_blank[q] blank_k).  The A fragments of each 16-key chunk are read from
 // the staged dS rows through the bias-run offset table (absent clusters hit a
 // zero block), so a chunk is two 32-bit loads per fragment half and four mma.
-template <typename T>
-__device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpDq<T>& w, int b, int h, int n0,
+template <typename T, int MM>
+__device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpDq<T, MM>& w, int b, int h, int n0,
                             int nq, int nclu) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int N = a.N, M = a.M;
@@ -529,7 +531,7 @@ __device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpDq<T>& 
   cp_commit();
   warp_load_k(w.K[0], kb, s.uclu, 0, nclu);
   cp_commit();
-  if (lane < 8) w.dS[BSENT + lane] = pos_zero<T>();
+  if (lane < 8) w.dS[TQ * MM + lane] = pos_zero<T>();
   float qacc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
@@ -567,25 +569,27 @@ __device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup& s, BlkWarpDq<T>& 
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(TC_THREADS) nbhd_blk_dq_kernel(NbhdArgs a) {
+template <typename T, int MM>
+__global__ void __launch_bounds__(TC_THREADS, AFFB_DQ_MINB) nbhd_blk_dq_kernel(NbhdArgs a) {
   if (*a.general) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  BlkDqSmem<T>& s = *reinterpret_cast<BlkDqSmem<T>*>(smem_raw);
+  BlkDqSmem<T, MM>& s = *reinterpret_cast<BlkDqSmem<T, MM>*>(smem_raw);
   const int N = a.N;
   const int tiles = (N + TQ - 1) / TQ;
   const int b = blockIdx.x / tiles;
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup(s.setup, a.midx, b, n0, nq, N, a.M);
+  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
   if (nclu < 0) return;  // excluded by the list check that cleared the flag
   const int warp = threadIdx.x >> 5;
-  for (int h = warp; h < a.H; h += NW) blk_dq_head<T>(a, s.setup, s.w[warp], b, h, n0, nq, nclu);
+  for (int h = warp; h < a.H; h += NW) blk_dq_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);
 }
 
 template <typename K>
 static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStream_t st) {
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
     set_error("nbhd_attn: cannot reserve %zu bytes of shared memory", smem);
     return AFFB_ERR_CUDA;
   }
@@ -594,19 +598,25 @@ static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStrea
   return AFFB_OK;
 }
 
-int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
-  if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_fwd_kernel<__nv_bfloat16>, sizeof(BlkFwdSmem<__nv_bfloat16>), a, B, st);
-  return launch_blk(nbhd_blk_fwd_kernel<__half>, sizeof(BlkFwdSmem<__half>), a, B, st);
-}
+// Neighbour capacity of the tile structures for M (a multiple of 8, <= 64).
+static int blk_mm(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
 
-int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
-  if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_bwd_kernel<__nv_bfloat16>, sizeof(BlkBwdSmem<__nv_bfloat16>), a, B, st);
-  return launch_blk(nbhd_blk_bwd_kernel<__half>, sizeof(BlkBwdSmem<__half>), a, B, st);
-}
+#define AFFB_BLK_LAUNCH(KERNEL, SMEM)                                                                     \
+  do {                                                                                                    \
+    switch (blk_mm(a.M)) {                                                                                \
+      case 16: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 16>, sizeof(SMEM<__nv_bfloat16, 16>), a, B, st) \
+                                         : launch_blk(KERNEL<__half, 16>, sizeof(SMEM<__half, 16>), a, B, st);             \
+      case 32: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 32>, sizeof(SMEM<__nv_bfloat16, 32>), a, B, st) \
+                                         : launch_blk(KERNEL<__half, 32>, sizeof(SMEM<__half, 32>), a, B, st);             \
+      case 48: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 48>, sizeof(SMEM<__nv_bfloat16, 48>), a, B, st) \
+                                         : launch_blk(KERNEL<__half, 48>, sizeof(SMEM<__half, 48>), a, B, st);             \
+      default: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 64>, sizeof(SMEM<__nv_bfloat16, 64>), a, B, st) \
+                                         : launch_blk(KERNEL<__half, 64>, sizeof(SMEM<__half, 64>), a, B, st);             \
+    }                                                                                                     \
+  } while (0)
 
-int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
-  if (dtype == AFFB_BF16) return launch_blk(nbhd_blk_dq_kernel<__nv_bfloat16>, sizeof(BlkDqSmem<__nv_bfloat16>), a, B, st);
-  return launch_blk(nbhd_blk_dq_kernel<__half>, sizeof(BlkDqSmem<__half>), a, B, st);
-}
+int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_fwd_kernel, BlkFwdSmem); }
+int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_bwd_kernel, BlkBwdSmem); }
+int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_dq_kernel, BlkDqSmem); }
 
 }  // namespace affb

@@ -254,15 +254,15 @@ int nbhd_q_prologue(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaSt
 
 template <typename T>
 struct KvWarp {
-  alignas(16) T K[8 * KST];
-  alignas(16) T V[8 * KST];
-  alignas(16) T Q[2][16 * KST];
-  alignas(16) T dO[2][16 * KST];
+  alignas(16) T K[8 * TD];
+  alignas(16) T V[8 * TD];
+  alignas(16) T Q[2][16 * TD];
+  alignas(16) T dO[2][16 * TD];
   alignas(16) T bias[2][16 * 8];
   alignas(16) uint8_t mask[2][16 * 8];
   alignas(16) float lse[2][16];
   alignas(16) float di[2][16];
-  alignas(16) T ost[8 * KST];
+  alignas(16) T ost[8 * TD];
 };
 // The block's list (or a segment of it) as per-entry offsets shared by the
 // heads: qoff = q * D (Q / dO rows), roff = q * M + 8 j (bias / mask / dS runs).
@@ -297,8 +297,8 @@ __device__ __forceinline__ void kv_stage(const KvHead<T>& p, const KvSmem<T>& s,
     const int row = i >> 2, piece = i & 3;
     const bool valid = row < nr;
     const int qo = (valid ? s.qoff[base + row] : 0) + piece * 8;
-    cp_async16(w.Q[buf] + row * KST + piece * 8, p.q + qo, valid);
-    cp_async16(w.dO[buf] + row * KST + piece * 8, p.dout + qo, valid);
+    cp_async16(w.Q[buf] + swz(row, piece), p.q + qo, valid);
+    cp_async16(w.dO[buf] + swz(row, piece), p.dout + qo, valid);
   }
   const int row = lane & 15;
   const bool valid = row < nr;
@@ -330,8 +330,8 @@ __device__ __forceinline__ void kv_segment(const NbhdArgs& a, const KvHead<T>& p
     cp_wait<1>();
     __syncwarp();
     if (!frags) {  // K / V rows of the cluster arrived with the first stage
-      ldsm_x4(bk, w.K + (lane & 7) * KST + (lane >> 3) * 8);
-      ldsm_x4(bv, w.V + (lane & 7) * KST + (lane >> 3) * 8);
+      ldsm_x4(bk, w.K + swz(lane & 7, lane >> 3));
+      ldsm_x4(bv, w.V + swz(lane & 7, lane >> 3));
       frags = true;
     }
     uint32_t aq[2][4], ado[2][4];
@@ -373,7 +373,7 @@ __device__ __forceinline__ void kv_segment(const NbhdArgs& a, const KvHead<T>& p
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
       // A[m = dim][k = query] = X[query][dim]: matrices (d 0-7, q 0-7), (d 8-15, q 0-7), (d 0-7, q 8-15), (d 8-15, q 8-15)
-      const int off = ((mi >> 1) * 8 + (lane & 7)) * KST + (mt * 2 + (mi & 1)) * 8;
+      const int off = swz((mi >> 1) * 8 + (lane & 7), mt * 2 + (mi & 1));
       uint32_t ad[4], aqt[4];
       ldsm_x4_t(ad, w.dO[buf] + off);
       ldsm_x4_t(aqt, w.Q[buf] + off);
@@ -458,8 +458,8 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_KV_MINB) nbhd_kv_kernel(NbhdA
       const int row = lane >> 2, piece = lane & 3;
       const bool valid = row < nkeys;
       const int64_t off = (bh * N + kr0 + (valid ? row : 0)) * TD + piece * 8;
-      cp_async16(w.K + row * KST + piece * 8, (const T*)a.k + off, valid);
-      cp_async16(w.V + row * KST + piece * 8, (const T*)a.v + off, valid);
+      cp_async16(w.K + swz(row, piece), (const T*)a.k + off, valid);
+      cp_async16(w.V + swz(row, piece), (const T*)a.v + off, valid);
     }
     for (int seg0 = 0; seg0 < n; seg0 += KV_LCAP) {
       const int ns = min(KV_LCAP, n - seg0);
@@ -477,13 +477,13 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_KV_MINB) nbhd_kv_kernel(NbhdA
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int d = mt * 16 + g + (e >> 1) * 8, key = 2 * tq + (e & 1);
-          io<T>::st(w.ost + key * KST + d, acc[mt][e] * mul);
+          io<T>::st(w.ost + swz(key, d >> 3) + (d & 7), acc[mt][e] * mul);
         }
       __syncwarp();
       const int row = lane >> 2, piece = lane & 3;
       if (row < nkeys) {
         T* dst = (T*)(pass == 0 ? k.dk : k.dv) + (bh * N + kr0 + row) * TD + piece * 8;
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(w.ost + row * KST + piece * 8);
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(w.ost + swz(row, piece));
       }
       __syncwarp();
     }
@@ -495,7 +495,9 @@ int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream
   if (blocks == 0) return AFFB_OK;
   AFFB_REQUIRE(blocks < (1ll << 31), "nbhd_attn_bwd: too many key clusters");
   auto go = [&](auto kernel, size_t smem) -> int {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
       set_error("nbhd_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
       return AFFB_ERR_CUDA;
     }

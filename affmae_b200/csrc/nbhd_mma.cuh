@@ -12,15 +12,21 @@ constexpr int TQ = 16;          // queries per tile
 constexpr int TD = 32;          // head dim
 constexpr int MMAX = 64;        // neighbours per query
 constexpr int TC_THREADS = 128;
-constexpr int KST = TD + 8;     // smem row stride (elements) of Q/K/V/dO tiles: 80 B
+// Q/K/V/dO tiles in shared memory: rows of TD elements (64 B, unpadded) with
+// the 16-byte chunks of row r stored in XOR order ch ^ ((r >> 1) & 3), so the
+// eight rows one ldmatrix reads fall in eight distinct bank groups.
+__device__ __forceinline__ int swz(int row, int ch) { return row * TD + ((ch ^ ((row >> 1) & 3)) << 3); }
 constexpr int NW = TC_THREADS / 32;
 
 // Minimum resident blocks per SM requested from the register allocator.
 #ifndef AFFB_FWD_MINB
-#define AFFB_FWD_MINB 1
+#define AFFB_FWD_MINB 7  // 72 registers: 7 forward tiles per SM
 #endif
 #ifndef AFFB_BWD_MINB
 #define AFFB_BWD_MINB 1
+#endif
+#ifndef AFFB_DQ_MINB
+#define AFFB_DQ_MINB 10  // 48 registers: 10 dQ tiles per SM
 #endif
 #ifndef AFFB_KV_MINB
 #define AFFB_KV_MINB 6  // 80 registers: 6 blocks of the key-side kernel per SM
@@ -93,7 +99,7 @@ __device__ __forceinline__ void mma_chunk_nt(float (*acc)[4], const uint32_t (*a
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     uint32_t bb[4];
-    ldsm_x4(bb, Bm + (u0 + j * 8 + (lane & 7)) * KST + (lane >> 3) * 8);
+    ldsm_x4(bb, Bm + swz(u0 + j * 8 + (lane & 7), lane >> 3));
     acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     MmaType<T>::mma(acc[j], a[0], bb);
     MmaType<T>::mma(acc[j], a[1], bb + 2);
@@ -109,7 +115,7 @@ __device__ __forceinline__ void mma_chunk_pv(float (*out)[4], const uint32_t* a,
     uint32_t bb[4];
     // matrices (u0-7, d), (u8-15, d), (u0-7, d+8), (u8-15, d+8)
     const int j = lane >> 3;
-    ldsm_x4_t(bb, X + (u0 + (j & 1) * 8 + (lane & 7)) * KST + dp * 16 + (j >> 1) * 8);
+    ldsm_x4_t(bb, X + swz(u0 + (j & 1) * 8 + (lane & 7), dp * 2 + (j >> 1)));
     MmaType<T>::mma(out[dp * 2], a, bb);
     MmaType<T>::mma(out[dp * 2 + 1], a, bb + 2);
   }
@@ -131,7 +137,7 @@ __device__ __forceinline__ void mma_chunk_scatter(const T* Pt, int pst, const T*
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
     uint32_t yb[2];
-    ldsm_x2_t(yb, Y + (lane & 15) * KST + nt * 8);
+    ldsm_x2_t(yb, Y + swz(lane & 15, nt));
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     MmaType<T>::mma(acc, a, yb);
     const int col = nt * 8 + 2 * tq;
@@ -145,7 +151,7 @@ __device__ __forceinline__ void load_a_frags(uint32_t (*a)[4], const T* A) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int ks = 0; ks < 2; ++ks)
-    ldsm_x4(a[ks], A + ((lane & 7) + ((lane >> 3) & 1) * 8) * KST + ks * 16 + (lane >> 4) * 8);
+    ldsm_x4(a[ks], A + swz((lane & 7) + ((lane >> 3) & 1) * 8, ks * 2 + (lane >> 4)));
 }
 
 template <typename T> __device__ __forceinline__ T neg_inf();
@@ -163,7 +169,7 @@ __device__ __forceinline__ void warp_load16(T* dst, const T* __restrict__ src, R
   for (int i = lane; i < 64; i += 32) {
     const int row = i >> 2, c = i & 3;
     const int64_t gr = rowof(row);
-    cp_async16(dst + row * KST + c * 8, src + (gr < 0 ? 0 : gr) * TD + c * 8, gr >= 0);
+    cp_async16(dst + swz(row, c), src + (gr < 0 ? 0 : gr) * TD + c * 8, gr >= 0);
   }
 }
 __device__ __forceinline__ void cp_async8(void* dst, const void* src, bool valid) {
@@ -196,8 +202,8 @@ __device__ __forceinline__ void rows_dot(const T* tile, const T* __restrict__ ve
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   float v[8], x0[8], x1[8];
   ld8(vec + tq * 8, v);
-  ld8_shared(tile + g * KST + tq * 8, x0);
-  ld8_shared(tile + (g + 8) * KST + tq * 8, x1);
+  ld8_shared(tile + swz(g, tq), x0);
+  ld8_shared(tile + swz(g + 8, tq), x1);
   d0 = 0.f; d1 = 0.f;
 #pragma unroll
   for (int e = 0; e < 8; ++e) { d0 = fmaf(x0[e], v[e], d0); d1 = fmaf(x1[e], v[e], d1); }

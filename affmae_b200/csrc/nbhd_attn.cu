@@ -74,12 +74,12 @@ static void dispatch_lpn(int64_t D, F&& f) {
 
 static NbhdArgs make_args(const void* q, const void* k, const void* v, const int32_t* mi,
                           const void* bias, const uint8_t* mask, int mask_heads, const void* bk,
-                          const void* bv, int64_t H, int64_t N, int64_t D, int64_t M, float scale) {
+                          const void* bv, int64_t B, int64_t H, int64_t N, int64_t D, int64_t M, float scale) {
   NbhdArgs a{};
   a.q = q; a.k = k; a.v = v; a.midx = mi; a.bias = bias; a.mask = mask;
   a.mask_heads = mask ? mask_heads : 1;
   a.blank_k = bk; a.blank_v = bv;
-  a.H = (int)H; a.N = (int)N; a.D = (int)D; a.M = (int)M; a.scale = scale;
+  a.B = (int)B; a.H = (int)H; a.N = (int)N; a.D = (int)D; a.M = (int)M; a.scale = scale;
   return a;
 }
 
@@ -95,7 +95,7 @@ extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
                                   float* lse, void* stream) {
   if (int e = check_na(B, H, N, D, M, mask ? mask_heads : 1, blank_k, blank_v, q, k, v)) return e;
   if (B == 0 || N == 0) return AFFB_OK;
-  NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, H, N, D, M, scale);
+  NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, B, H, N, D, M, scale);
   a.out = out;
   a.lse = lse;
   cudaStream_t st = as_stream(stream);
@@ -148,7 +148,7 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
   AFFB_REQUIRE(ly.total == 0 || workspace, "nbhd_attn_bwd: workspace is NULL");
   if (B == 0 || N == 0) return AFFB_OK;
   AFFB_REQUIRE(B * N * (M / 8) < (1ll << 31), "nbhd_attn_bwd: too many list entries");
-  NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, H, N, D, M, scale);
+  NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, B, H, N, D, M, scale);
   a.o = o; a.dout = dout; a.lse = const_cast<float*>(lse);
   a.dq = dq; a.dbias = bias ? dbias : nullptr;
   a.dbk = dbk_acc; a.dbv = dbv_acc;

@@ -492,19 +492,24 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel
   BlkBwdSmem<T, MM>& s = *reinterpret_cast<BlkBwdSmem<T, MM>*>(smem_raw);
   const int N = a.N;
   const int tiles = (N + TQ - 1) / TQ;
-  const int b = blockIdx.x / tiles;
-  const int n0 = (blockIdx.x % tiles) * TQ;
-  const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
   const int warp = threadIdx.x >> 5;
-  if (nclu < 0) {  // not cluster-block lists: CUDA-core rows, blank-token grads straight to global
-    for (int w = warp; w < a.H * nq; w += NW) {
-      const int h = w / nq;
-      nbhd_bwd_row<T, 4>(a, b, h, n0 + w % nq, a.dbk + (int64_t)h * TD, a.dbv + (int64_t)h * TD);
+  // grid-stride over tiles: the launch is small so that the common case (flag
+  // clear) costs one wave of blocks that return at once
+  for (int64_t tile = blockIdx.x; tile < (int64_t)tiles * a.B; tile += gridDim.x) {
+    const int b = (int)(tile / tiles);
+    const int n0 = (int)(tile % tiles) * TQ;
+    const int nq = min(TQ, N - n0);
+    __syncthreads();  // the previous tile's warps are done with shared memory
+    const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
+    if (nclu < 0) {  // not cluster-block lists: CUDA-core rows, blank-token grads straight to global
+      for (int w = warp; w < a.H * nq; w += NW) {
+        const int h = w / nq;
+        nbhd_bwd_row<T, 4>(a, b, h, n0 + w % nq, a.dbk + (int64_t)h * TD, a.dbv + (int64_t)h * TD);
+      }
+      continue;
     }
-    return;
+    for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);
   }
-  for (int h = warp; h < a.H; h += NW) blk_bwd_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);
 }
 
 // dQ of one head and tile from dS, which the key-side kernel has written in
@@ -586,14 +591,15 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_DQ_MINB) nbhd_blk_dq_kernel(N
 }
 
 template <typename K>
-static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStream_t st) {
+static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStream_t st, int64_t max_blocks = 0) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
       cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                            (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
     set_error("nbhd_attn: cannot reserve %zu bytes of shared memory", smem);
     return AFFB_ERR_CUDA;
   }
-  const int64_t tiles = (int64_t)((a.N + TQ - 1) / TQ) * B;
+  int64_t tiles = (int64_t)((a.N + TQ - 1) / TQ) * B;
+  if (max_blocks > 0 && tiles > max_blocks) tiles = max_blocks;
   kernel<<<(unsigned)tiles, TC_THREADS, smem, st>>>(a);
   return AFFB_OK;
 }
@@ -601,22 +607,24 @@ static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStrea
 // Neighbour capacity of the tile structures for M (a multiple of 8, <= 64).
 static int blk_mm(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
 
-#define AFFB_BLK_LAUNCH(KERNEL, SMEM)                                                                     \
+#define AFFB_BLK_LAUNCH(KERNEL, SMEM, MAXB)                                                                   \
   do {                                                                                                    \
     switch (blk_mm(a.M)) {                                                                                \
-      case 16: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 16>, sizeof(SMEM<__nv_bfloat16, 16>), a, B, st) \
-                                         : launch_blk(KERNEL<__half, 16>, sizeof(SMEM<__half, 16>), a, B, st);             \
-      case 32: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 32>, sizeof(SMEM<__nv_bfloat16, 32>), a, B, st) \
-                                         : launch_blk(KERNEL<__half, 32>, sizeof(SMEM<__half, 32>), a, B, st);             \
-      case 48: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 48>, sizeof(SMEM<__nv_bfloat16, 48>), a, B, st) \
-                                         : launch_blk(KERNEL<__half, 48>, sizeof(SMEM<__half, 48>), a, B, st);             \
-      default: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 64>, sizeof(SMEM<__nv_bfloat16, 64>), a, B, st) \
-                                         : launch_blk(KERNEL<__half, 64>, sizeof(SMEM<__half, 64>), a, B, st);             \
+      case 16: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 16>, sizeof(SMEM<__nv_bfloat16, 16>), a, B, st, MAXB) \
+                                         : launch_blk(KERNEL<__half, 16>, sizeof(SMEM<__half, 16>), a, B, st, MAXB);             \
+      case 32: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 32>, sizeof(SMEM<__nv_bfloat16, 32>), a, B, st, MAXB) \
+                                         : launch_blk(KERNEL<__half, 32>, sizeof(SMEM<__half, 32>), a, B, st, MAXB);             \
+      case 48: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 48>, sizeof(SMEM<__nv_bfloat16, 48>), a, B, st, MAXB) \
+                                         : launch_blk(KERNEL<__half, 48>, sizeof(SMEM<__half, 48>), a, B, st, MAXB);             \
+      default: return dtype == AFFB_BF16 ? launch_blk(KERNEL<__nv_bfloat16, 64>, sizeof(SMEM<__nv_bfloat16, 64>), a, B, st, MAXB) \
+                                         : launch_blk(KERNEL<__half, 64>, sizeof(SMEM<__half, 64>), a, B, st, MAXB);             \
     }                                                                                                     \
   } while (0)
 
-int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_fwd_kernel, BlkFwdSmem); }
-int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_bwd_kernel, BlkBwdSmem); }
-int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_dq_kernel, BlkDqSmem); }
+int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_fwd_kernel, BlkFwdSmem, 0); }
+int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {
+  AFFB_BLK_LAUNCH(nbhd_blk_bwd_kernel, BlkBwdSmem, 2 * sm_count());
+}
+int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_dq_kernel, BlkDqSmem, 0); }
 
 }  // namespace affb

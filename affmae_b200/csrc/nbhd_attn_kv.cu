@@ -51,10 +51,10 @@ __global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, i
                                       int* __restrict__ flag, int* __restrict__ counts,
                                       int* __restrict__ ecl, int* __restrict__ erk) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= (int64_t)B * N) return;
-  const int b = (int)(t / N);
+  const bool valid = t < (int64_t)B * N;
+  const int b = valid ? (int)(t / N) : 0;
   const int J = M >> 3;
-  const int4* row = reinterpret_cast<const int4*>(midx + t * M);
+  const int4* row = reinterpret_cast<const int4*>(midx + (valid ? t : 0) * M);
   int4 x[8], y[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j)
@@ -63,7 +63,7 @@ __global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, i
   bool ok = true;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    cs[j] = -1;
+    cs[j] = 0;
     if (j < J) {
       const int c0 = x[j].x;
       ok &= (c0 >= 0) & ((c0 & 7) == 0) & (c0 <= N - 8) & (x[j].y == c0 + 1) & (x[j].z == c0 + 2) &
@@ -73,15 +73,24 @@ __global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, i
       for (int jj = 0; jj < j; ++jj) ok &= cs[jj] != cs[j];
     }
   }
-  if (!ok) {
-    *reinterpret_cast<volatile int*>(flag) = 1;
-    return;
-  }
+  if (valid && !ok) *reinterpret_cast<volatile int*>(flag) = 1;
+  // Queries of one warp are neighbours and list mostly the same clusters: one
+  // atomic per distinct cluster and warp, ranks in lane order.
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    if (j < J) {
-      ecl[t * J + j] = cs[j];
-      erk[t * J + j] = atomicAdd(counts + (int64_t)b * Cc + cs[j], 1);
+    if (j < J) {  // J is uniform: every lane takes part in the match
+      const bool use = valid && ok;
+      const int key = use ? b * Cc + cs[j] : -1 - lane;
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      const int leader = __ffs(peers) - 1;
+      int base = 0;
+      if (use && lane == leader) base = atomicAdd(counts + key, __popc(peers));
+      base = __shfl_sync(0xffffffffu, base, leader);
+      if (use) {
+        ecl[t * J + j] = cs[j];
+        erk[t * J + j] = base + __popc(peers & ((1u << lane) - 1u));
+      }
     }
   }
 }

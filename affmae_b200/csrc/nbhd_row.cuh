@@ -56,7 +56,7 @@ struct NbhdArgs {
   int mask_heads;
   const void* blank_k;
   const void* blank_v;
-  int H, N, D, M;
+  int B, H, N, D, M;
   float scale;
   // forward outputs
   void* out;

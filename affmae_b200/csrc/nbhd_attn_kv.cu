@@ -407,12 +407,18 @@ __device__ __forceinline__ void kv_load_segment(KvSmem<T>& s, const int* src, in
     }
   } else {  // rank sort (entries are distinct); before any staging, so a Q stage holds the copy
     int* tmp = reinterpret_cast<int*>(s.w[0].Q);
-    for (int i = t; i < ns; i += TC_THREADS) tmp[i] = src[i];
+    const int n4 = (ns + 3) >> 2;  // padded with INT_MAX, which no entry exceeds
+    for (int i = t; i < 4 * n4; i += TC_THREADS) tmp[i] = i < ns ? src[i] : 0x7fffffff;
     __syncthreads();
+    const int4* t4 = reinterpret_cast<const int4*>(tmp);
     for (int i = t; i < ns; i += TC_THREADS) {
       const int e = tmp[i];
       int r = 0;
-      for (int m = 0; m < ns; ++m) r += tmp[m] < e;
+#pragma unroll 4
+      for (int m = 0; m < n4; ++m) {
+        const int4 v = t4[m];
+        r += (v.x < e) + (v.y < e) + (v.z < e) + (v.w < e);
+      }
       s.qoff[r] = (e >> 3) * TD;
       s.roff[r] = (e >> 3) * M + 8 * (e & 7);
     }

@@ -93,8 +93,13 @@ def lib():
         return l
 
 
+CALLS = 0  # entry-point calls made by this process (the benchmark reports them per step)
+
+
 def call(name: str, *args) -> None:
     """Call an entry point; raise RuntimeError carrying the library's message."""
+    global CALLS
+    CALLS += 1
     rc = getattr(lib(), name)(*args)
     if rc != 0:
         msg = lib().affb_last_error().decode(errors="replace")

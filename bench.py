@@ -112,6 +112,8 @@ def dist_setup():
     if world > 1:
         import torch.distributed as dist
         backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
         dist.init_process_group(backend=backend)
     return world, rank, local
 
@@ -354,6 +356,73 @@ def run_gpu(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_mae(args, world, rank, local):
+    """Config 5: AFF-small MAE pretraining steps, data parallel over `world`
+    GPUs (DDP, NCCL all-reduce overlapped with the backward pass)."""
+    from affmae_b200 import _native as nat
+    from affmae_b200.mae import MAEConfig
+    from affmae_b200.pretrain import build, synthetic_images, train_step
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = MAEConfig()
+    per_gpu = args.mae_batch
+    model, opt = build(cfg, device=dev, ddp=world > 1, seed=0)
+    imgs = synthetic_images(per_gpu, cfg.img_size, seed=1000 + rank, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        train_step(model, opt, imgs, generator=gen)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    calls0 = nat.CALLS
+    with ClockSampler(local) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            loss = train_step(model, opt, imgs, generator=gen)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        calls = nat.CALLS - calls0
+        dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+        barrier(world)
+        # e2e: every step copies its images from pinned host memory and reads the loss back
+        host = imgs.cpu().pin_memory()
+        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+        torch.cuda.synchronize()
+        barrier(world)
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(args.steps):
+            x = host.to(dev, non_blocking=True)
+            loss = train_step(model, opt, x, generator=gen)
+            loss_host.copy_(loss.float(), non_blocking=True)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(e2.elapsed_time(e3) / 1e3, world)
+    clocks = clk.summary()
+    if rank == 0:
+        value = world * per_gpu * args.steps / dev_s
+        line = {"metric": "AFF-small MAE pretraining img/s", "value": value, "unit": "img/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic N(0,1) images, normalised per image; random-init weights",
+                "config": {"workload": "AFF-small MAE pretraining step (config 5)", "global_batch": per_gpu * world,
+                           "per_gpu_batch": per_gpu, "img_size": cfg.img_size, "patch": cfg.patch_size,
+                           "mask_ratio": cfg.mask_ratio, "nbhd": cfg.nbhd_size, "parallelism": f"ddp{world}",
+                           "l2": "working set far above L2 (no flush needed)"},
+                "img_per_s_per_gpu": value / world, "final_loss": float(loss),
+                "e2e": {"value": world * per_gpu * args.steps / e2e_s, "unit": "img/s",
+                        "h2d_bytes_per_step": host.numel() * host.element_size(), "d2h_bytes_per_step": 4,
+                        "ms_per_step": e2e_s * 1e3 / args.steps},
+                "roofline": None, "cpu_baseline": None,
+                "cpu_baseline_note": "not run for config 5 (a CPU pretraining step is infeasible)",
+                "clocks": clocks, "abi_calls_per_step": calls / args.steps}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -363,10 +432,20 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--batch", type=int, default=CFG["B"], help="images per GPU (default: config 3's 32)")
+    ap.add_argument("--workload", default="attn", choices=["attn", "mae"],
+                    help="attn: config 3 neighbourhood attention (default); mae: config 5 pretraining")
+    ap.add_argument("--mae-batch", type=int, default=16, help="images per GPU for --workload mae")
     args = ap.parse_args()
     CFG["B"] = args.batch
     world, rank, local = dist_setup()
-    if args.impl == "reference":
+    if args.workload == "mae":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference's MAE model needs its Triton "
+                                  "GPU kernels and pykeops, which are not installed on the GPU box"}), flush=True)
+        else:
+            run_mae(args, world, rank, local)
+    elif args.impl == "reference":
         run_reference(args, world, rank)
     else:
         run_gpu(args, world, rank, local)

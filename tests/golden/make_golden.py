@@ -218,13 +218,48 @@ def gen_ms(R):
         d_val=d_val)
 
 
+def gen_clusters(R):
+    """The model's token clustering, src/utils/geometry.py:170-319, loaded with
+    a stub for the pykeops import at the top of that file (unused by it)."""
+    root = R["_root"]
+    sys.modules.setdefault("pykeops", types.ModuleType("pykeops"))
+    pk = types.ModuleType("pykeops.torch")
+    pk.LazyTensor = None
+    sys.modules.setdefault("pykeops.torch", pk)
+    # geometry.py also imports two kernel wrappers that space_filling_cluster does not use
+    for name, attr in [("src", None), ("src.layers", None), ("src.layers.kernels", None),
+                       ("src.layers.kernels.weighted_gather", "weighted_gather"),
+                       ("src.layers.kernels.knn", "knn")]:
+        mod = sys.modules.setdefault(name, types.ModuleType(name))
+        if attr:
+            setattr(mod, attr, None)
+    spec = importlib.util.spec_from_file_location("refgeom", os.path.join(root, "src", "utils", "geometry.py"))
+    geo = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(geo)
+    g = torch.Generator().manual_seed(7)
+    cases = {}
+    # on-grid 32x32; half of a 64x64 grid in random order; 1021 tokens of it (padded last cluster)
+    ys, xs = torch.meshgrid(torch.arange(32), torch.arange(32), indexing="ij")
+    cases["grid"] = (torch.stack([xs, ys], -1).reshape(1, -1, 2).float().repeat(2, 1, 1), 32)
+    ys, xs = torch.meshgrid(torch.arange(64), torch.arange(64), indexing="ij")
+    full = torch.stack([xs, ys], -1).reshape(-1, 2).float()
+    half = torch.stack([full[torch.randperm(4096, generator=g)[:2048]] for _ in range(2)])
+    cases["half"] = (half, 64)
+    cases["ragged"] = (half[:, :1021].contiguous(), 64)
+    for tag, (pos, hw) in cases.items():
+        p2, means, member, cmask, order = geo.space_filling_cluster(pos, 8, hw, hw, no_reorder=False)
+        npz(f"clusters_{tag}", pos=pos, hw=hw, pos_out=p2, means=means, member=member, order=order.squeeze(2),
+            cmask=cmask if cmask is not None else np.zeros(0))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE", "/root/reference"))
     a = ap.parse_args()
     R = load_reference(a.reference)
+    R["_root"] = a.reference
     torch.set_num_threads(1)
-    for fn in [gen_knn, gen_local_attn, gen_weighted, gen_deform, gen_ms][int(os.environ.get("GOLDEN_FROM", "0")):]:
+    for fn in [gen_knn, gen_local_attn, gen_weighted, gen_deform, gen_ms, gen_clusters][int(os.environ.get("GOLDEN_FROM", "0")):]:
         t = time.time()
         print(fn.__name__, flush=True)
         fn(R)

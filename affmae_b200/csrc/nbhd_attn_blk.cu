@@ -82,12 +82,23 @@ template <typename T, int MM> using BlkFwdSmem = BlkSmem<MM, BlkWarpFwd<T, MM>>;
 template <typename T, int MM> using BlkBwdSmem = BlkSmem<MM, BlkWarpBwd<T, MM>>;
 template <typename T, int MM> using BlkDqSmem = BlkSmem<MM, BlkWarpDq<T, MM>>;
 
+// True when list column `col` of query n is masked (mask == 0) in every mask
+// head: the only form in which a run may extend past the last token.
+__device__ __forceinline__ bool run_slot_masked(const NbhdArgs& a, int b, int n, int col) {
+  if (!a.mask) return false;
+  for (int hm = 0; hm < a.mask_heads; ++hm)
+    if (a.mask[(((int64_t)b * a.mask_heads + hm) * a.N + n) * a.M + col] != 0) return false;
+  return true;
+}
+
 __device__ __forceinline__ uint32_t clu_slot(int key) { return ((uint32_t)key * 2654435761u) >> 24; }
 
 // Checks the cluster-block form of the tile and builds its cluster union.
 // Returns the number of clusters, or -1 when the tile needs the general path.
 template <int MM>
-__device__ int blk_setup(BlkSetup<MM>& s, int* sidx, const int32_t* __restrict__ midx, int b, int n0, int nq, int N, int M) {
+__device__ int blk_setup(BlkSetup<MM>& s, int* sidx, const NbhdArgs& a, int b, int n0, int nq) {
+  const int N = a.N, M = a.M;
+  const int32_t* __restrict__ midx = a.midx;
   const int t = threadIdx.x;
   const int J = M >> 3;  // clusters per list
   {
@@ -111,9 +122,10 @@ __device__ int blk_setup(BlkSetup<MM>& s, int* sidx, const int32_t* __restrict__
   if (q < nq && j < J) {
     const int* run = sidx + q * M + 8 * j;
     const int c0 = run[0];
-    bool ok = c0 >= 0 && (c0 & 7) == 0 && c0 + 8 <= N;
+    bool ok = c0 >= 0 && (c0 & 7) == 0 && c0 < N;
 #pragma unroll
-    for (int r = 1; r < 8; ++r) ok = ok && run[r] == c0 + r;
+    for (int r = 1; r < 8; ++r)  // past the last token: a masked padding slot of a partial last cluster
+      ok = ok && (c0 + r < N ? run[r] == c0 + r : run_slot_masked(a, b, n0 + q, 8 * j + r));
     for (int jj = 0; jj < j; ++jj) ok = ok && sidx[q * M + 8 * jj] != c0;  // listed twice in one row
     if (ok) {
       cid = c0 >> 3;
@@ -195,14 +207,16 @@ __device__ __forceinline__ void bias_at(const T* sb, int bo, int tq, float& b0, 
 
 // cp.async of the K rows of cluster slots 2c, 2c+1 (16 keys), zeros past nclu.
 template <typename T>
-__device__ __forceinline__ void warp_load_k(T* dk, const T* __restrict__ kb, const int* uclu, int c, int nclu) {
+__device__ __forceinline__ void warp_load_k(T* dk, const T* __restrict__ kb, const int* uclu, int c, int nclu,
+                                            int N) {
   const int lane = threadIdx.x & 31;
   const int r = lane >> 2, piece = lane & 3;
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     const int u = 2 * c + hh;
-    const bool ok = u < nclu;
-    const int64_t src = (int64_t)(ok ? uclu[u] * 8 + r : 0) * TD + piece * 8;
+    const int key = u < nclu ? uclu[u] * 8 + r : N;
+    const bool ok = key < N;  // rows past the last token (partial last cluster) read as zeros
+    const int64_t src = (int64_t)(ok ? key : 0) * TD + piece * 8;
     cp_async16(dk + swz(hh * 8 + r, piece), kb + src, ok);
   }
 }
@@ -210,14 +224,15 @@ __device__ __forceinline__ void warp_load_k(T* dk, const T* __restrict__ kb, con
 // cp.async of the K and V rows of cluster slots 2c, 2c+1 (16 keys), zeros past nclu.
 template <typename T>
 __device__ __forceinline__ void warp_load_kv(T* dk, T* dv, const T* __restrict__ kb, const T* __restrict__ vb,
-                                             const int* uclu, int c, int nclu) {
+                                             const int* uclu, int c, int nclu, int N) {
   const int lane = threadIdx.x & 31;
   const int r = lane >> 2, piece = lane & 3;
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     const int u = 2 * c + hh;
-    const bool ok = u < nclu;
-    const int64_t src = (int64_t)(ok ? uclu[u] * 8 + r : 0) * TD + piece * 8;
+    const int key = u < nclu ? uclu[u] * 8 + r : N;
+    const bool ok = key < N;  // rows past the last token (partial last cluster) read as zeros
+    const int64_t src = (int64_t)(ok ? key : 0) * TD + piece * 8;
     const int dst = swz(hh * 8 + r, piece);
     cp_async16(dk + dst, kb + src, ok);
     cp_async16(dv + dst, vb + src, ok);
@@ -237,7 +252,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpFw
   warp_load16(w.Q, (const T*)a.q + (bh * N + n0) * TD, [=](int i) -> int64_t { return i < nq ? i : -1; });
   if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
   cp_commit();
-  warp_load_kv(w.KV[0][0], w.KV[0][1], kb, vb, uclu, 0, nclu);
+  warp_load_kv(w.KV[0][0], w.KV[0][1], kb, vb, uclu, 0, nclu, N);
   cp_commit();
   const uint8_t* mrow = a.mask ? a.mask + (((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N + n0) * M : nullptr;
   int ex[2] = {0, 0};
@@ -270,7 +285,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpFw
   for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   for (int c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
-    if (c + 1 < nchunk) warp_load_kv(w.KV[buf ^ 1][0], w.KV[buf ^ 1][1], kb, vb, uclu, c + 1, nclu);
+    if (c + 1 < nchunk) warp_load_kv(w.KV[buf ^ 1][0], w.KV[buf ^ 1][1], kb, vb, uclu, c + 1, nclu, N);
     cp_commit();
     cp_wait<1>();
     __syncwarp();
@@ -350,7 +365,7 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_FWD_MINB) nbhd_blk_fwd_kernel
   const int b = blockIdx.x / tiles;
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
+  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a, b, n0, nq);
   const int warp = threadIdx.x >> 5;
   if (nclu < 0) {  // not cluster-block lists: CUDA-core rows
     for (int w = warp; w < a.H * nq; w += NW) nbhd_fwd_row<T, 4>(a, b, w / nq, n0 + w % nq);
@@ -377,7 +392,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpBw
   warp_load16(w.dO, (const T*)a.dout + (bh * N + n0) * TD, rows_q);
   if (a.bias) warp_stage_bias(w.bias, a, b, h, n0, nq);
   cp_commit();
-  warp_load_kv(w.KV[0][0], w.KV[0][1], kb, vb, uclu, 0, nclu);
+  warp_load_kv(w.KV[0][0], w.KV[0][1], kb, vb, uclu, 0, nclu, N);
   cp_commit();
   const uint8_t* mrow = a.mask ? a.mask + (((int64_t)b * a.mask_heads + (a.mask_heads == 1 ? 0 : h)) * N + n0) * M : nullptr;
   float dl[2], ls[2];
@@ -432,7 +447,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpBw
   for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
   for (int c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
-    if (c + 1 < nchunk) warp_load_kv(w.KV[buf ^ 1][0], w.KV[buf ^ 1][1], kb, vb, uclu, c + 1, nclu);
+    if (c + 1 < nchunk) warp_load_kv(w.KV[buf ^ 1][0], w.KV[buf ^ 1][1], kb, vb, uclu, c + 1, nclu, N);
     cp_commit();
     cp_wait<1>();
     __syncwarp();
@@ -500,7 +515,7 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel
     const int n0 = (int)(tile % tiles) * TQ;
     const int nq = min(TQ, N - n0);
     __syncthreads();  // the previous tile's warps are done with shared memory
-    const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
+    const int nclu = blk_setup<MM>(s.setup, s.u.idx, a, b, n0, nq);
     if (nclu < 0) {  // not cluster-block lists: CUDA-core rows, blank-token grads straight to global
       for (int w = warp; w < a.H * nq; w += NW) {
         const int h = w / nq;
@@ -534,7 +549,7 @@ __device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpDq<
     }
   }
   cp_commit();
-  warp_load_k(w.K[0], kb, s.uclu, 0, nclu);
+  warp_load_k(w.K[0], kb, s.uclu, 0, nclu, N);
   cp_commit();
   if (lane < 8) w.dS[TQ * MM + lane] = pos_zero<T>();
   float qacc[4][4];
@@ -542,7 +557,7 @@ __device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpDq<
   for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
   for (int c = 0; c < nchunk; ++c) {
     const int buf = c & 1;
-    if (c + 1 < nchunk) warp_load_k(w.K[buf ^ 1], kb, s.uclu, c + 1, nclu);
+    if (c + 1 < nchunk) warp_load_k(w.K[buf ^ 1], kb, s.uclu, c + 1, nclu, N);
     cp_commit();
     cp_wait<1>();
     __syncwarp();
@@ -584,7 +599,7 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_DQ_MINB) nbhd_blk_dq_kernel(N
   const int b = blockIdx.x / tiles;
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a.midx, b, n0, nq, N, a.M);
+  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a, b, n0, nq);
   if (nclu < 0) return;  // excluded by the list check that cleared the flag
   const int warp = threadIdx.x >> 5;
   for (int h = warp; h < a.H; h += NW) blk_dq_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);

@@ -7,7 +7,9 @@
 // DK / DV).  Here the lists are inverted once per call instead:
 //   inv_count  one thread per query: checks that its list is M/8 runs of 8
 //              consecutive keys starting at a multiple of 8 with no cluster
-//              listed twice (the same test as the query-side tile setup),
+//              listed twice, where a run of the partial last cluster may end
+//              in padding slots masked in every mask head (the same test as
+//              the query-side tile setup),
 //              counts the queries that list each key cluster and remembers
 //              the rank of every (query, run) entry;
 //   inv_scan   one block per image: exclusive scan of the counts;
@@ -47,12 +49,14 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid
 
 // ---------------------------------------------------------------- lists --
 
-__global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, int N, int M, int Cc,
+__global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, const uint8_t* __restrict__ mask,
+                                      int mask_heads, int B, int N, int M, int Cc,
                                       int* __restrict__ flag, int* __restrict__ counts,
                                       int* __restrict__ ecl, int* __restrict__ erk) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = t < (int64_t)B * N;
   const int b = valid ? (int)(t / N) : 0;
+  const int64_t qn = valid ? t - (int64_t)b * N : 0;  // query index within its image
   const int J = M >> 3;
   const int4* row = reinterpret_cast<const int4*>(midx + (valid ? t : 0) * M);
   int4 x[8], y[8];
@@ -66,8 +70,19 @@ __global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, int B, i
     cs[j] = 0;
     if (j < J) {
       const int c0 = x[j].x;
-      ok &= (c0 >= 0) & ((c0 & 7) == 0) & (c0 <= N - 8) & (x[j].y == c0 + 1) & (x[j].z == c0 + 2) &
-            (x[j].w == c0 + 3) & (y[j].x == c0 + 4) & (y[j].y == c0 + 5) & (y[j].z == c0 + 6) & (y[j].w == c0 + 7);
+      const int v[8] = {x[j].x, x[j].y, x[j].z, x[j].w, y[j].x, y[j].y, y[j].z, y[j].w};
+      ok &= (c0 >= 0) & ((c0 & 7) == 0) & (c0 < N);
+#pragma unroll
+      for (int r = 1; r < 8; ++r) {
+        if (c0 + r < N) {
+          ok &= v[r] == c0 + r;
+        } else {  // past the last token: must be a padding slot masked in every mask head
+          bool masked = mask != nullptr;
+          for (int hm = 0; hm < mask_heads && masked; ++hm)
+            masked = mask[(((int64_t)b * mask_heads + hm) * N + qn) * M + 8 * j + r] == 0;
+          ok &= masked;
+        }
+      }
       cs[j] = c0 >> 3;
 #pragma unroll
       for (int jj = 0; jj < j; ++jj) ok &= cs[jj] != cs[j];
@@ -531,7 +546,8 @@ int nbhd_inv_lists(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, 
     return AFFB_ERR_CUDA;
   }
   const unsigned g = (unsigned)((rows + 255) / 256);
-  nbhd_inv_count_kernel<<<g, 256, 0, st>>>(a.midx, B, N, M, Cc, ly.flag, ly.counts, ly.ecl, ly.erk);
+  nbhd_inv_count_kernel<<<g, 256, 0, st>>>(a.midx, a.mask, a.mask_heads, B, N, M, Cc, ly.flag, ly.counts,
+                                           ly.ecl, ly.erk);
   nbhd_inv_scan_kernel<<<B, 1024, 0, st>>>(ly.counts, N, M >> 3, Cc, ly.flag, ly.offs);
   nbhd_inv_fill_kernel<<<g, 256, 0, st>>>(B, N, M, Cc, a.H, ly.flag, ly.offs, ly.ecl, ly.erk, ly.entries,
                                           ly.acc_k, ly.acc_v);

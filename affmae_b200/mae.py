@@ -217,7 +217,9 @@ class ClusterMerging(nn.Module):
         if mask is not None:
             lp = lp * mask.gather(1, sel)[..., None]
         table = self.weight_net(self.rel_table.to(feat.dtype))           # [T, inner]
-        weights = table[pe] * lp                                          # [B,keep,M,inner]
+        # gather through the bias kernel ([B,inner,keep,M]); its backward is one
+        # block-reduced scatter-add into the table instead of a sorted index_put
+        weights = pos_bias_gather(table, pe).permute(0, 2, 3, 1) * lp     # [B,keep,M,inner]
         merged = weighted_features(weights.to(feat.dtype), feat, member)  # [B,keep,inner,C]
         return pos_down, self.linear(self.norm(merged.reshape(B, keep, -1)))
 

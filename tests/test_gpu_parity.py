@@ -488,3 +488,36 @@ def test_nbhd_bwd_workspace_checked(cuda):
                  lse.data_ptr(), mi.data_ptr(), None, None, 1, None, None, nat.BF16, B, H, N, D, M, 1.0,
                  t.data_ptr(), t.data_ptr(), t.data_ptr(), None, None, None, ws.data_ptr(), need - 1,
                  nat.stream(t.device))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_local_attn_partial_last_cluster(cuda, dtype):
+    """The model's lists when N % 8 != 0: the last cluster is partial and its
+    padding slots point at token 0 with mask 0 (cluster-run fast path), plus the
+    same lists with one padding slot left unmasked (general path)."""
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    from affmae_b200.mae import curve_clusters, neighbourhood
+    g = golden("clusters_ragged")
+    pos, means, cmask, _ = curve_clusters(g["pos"].to(cuda), 8, 64, 64)
+    member, mask, _ = neighbourhood(pos, means, cmask, 48, 8)
+    B, N, M = member.shape
+    inp = _attn_inputs(B, 2, N, 32, M, dtype, mask=False, seed=21)
+    inp["mi"] = member.cpu().to(torch.int32)
+    for variant in ("masked", "unmasked_slot"):
+        m = mask.clone()
+        if variant == "unmasked_slot":
+            pad = (~m).nonzero()
+            m[tuple(pad[0])] = True
+        inp["mask"] = m.cpu()[:, None]
+        G = _to(inp, cuda)
+        kw = lambda d: dict(bias=d["bias"], mask=d["mask"], blank_k=d["blank_k"], blank_v=d["blank_v"])
+        o, lse = launch_flash_nbhood_attn_fwd(G["q"], G["k"], G["v"], G["mi"], 32 ** -0.5, **kw(G))
+        ro, rlse = oracle.nbhd_attn_fwd(inp["q"], inp["k"], inp["v"], inp["mi"], 32 ** -0.5, **kw(inp))
+        assert rel_err(o.cpu(), ro) < TOL_LP, variant
+        assert rel_err(lse.cpu(), rlse) < 1e-3, variant
+        grads = launch_flash_nbhood_attn_bwd(G["q"], G["k"], G["v"], G["mi"], 32 ** -0.5, o, lse, G["do"], **kw(G))
+        ref = oracle.nbhd_attn_bwd(inp["q"], inp["k"], inp["v"], inp["mi"], 32 ** -0.5, o.cpu(), lse.cpu(),
+                                   inp["do"], **kw(inp))
+        for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
+            assert rel_err(a.cpu(), b) < TOL_LP, (variant, name)

@@ -36,6 +36,8 @@ SIGNATURES = {
     "affb_nbhd_attn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _p, _p, _i32, _i64, _i64,
                            _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "affb_pos_bias_fwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
+    "affb_rel_bias_fwd": [_p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p],
+    "affb_rel_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p],
     "affb_pos_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "affb_deform_knn_fwd": [_p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p,
                             _p, _p, _p],

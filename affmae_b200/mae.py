@@ -9,8 +9,8 @@ on its path runs on this package's CUDA kernels:
   * tokens are grouped into clusters of 8 along a space-filling scan of grid
     anchors (``curve_clusters``; reference src/utils/geometry.py:170-319), each
     token attends the members of its 6 nearest clusters (KNN kernel) with a
-    relative-position bias (bias-gather kernel) and a blank token
-    (neighbourhood-attention kernels);
+    relative-position bias evaluated in-kernel from the Linear(5 -> H) weights
+    (relative-bias kernels) and a blank token (neighbourhood-attention kernels);
   * adaptive downsampling keeps the tokens with the highest learned
     importance and merges each kept token's neighbourhood with
     position-dependent weights (weighted-features kernels);
@@ -37,7 +37,7 @@ from .kernels.fused_deform_attn import (fused_knn_deformable_cross_attention,
                                         fused_knn_deformable_self_attention)
 from .kernels.knn import knn
 from .kernels.local_attn import FlashLocalAttentionFunction
-from .kernels.pos_bias import pos_bias_gather
+from .kernels.pos_bias import pos_bias_gather, rel_pos_bias
 from .kernels.weighted_features import weighted_features
 from .workloads import REL_POS_WIDTH, TABLE_WIDTH, relative_position_table
 
@@ -159,7 +159,6 @@ class ClusterAttention(nn.Module):
         self.blank_v = nn.Parameter(torch.randn(dim) * 0.2)
         self.pos_embed = nn.Linear(5, heads)
         self.proj = nn.Linear(dim, dim)
-        self.register_buffer("rel_table", relative_position_table(), persistent=False)
 
     def forward(self, feat, member_idx, mask, pe_idx):
         B, N, C = feat.shape
@@ -167,7 +166,7 @@ class ClusterAttention(nn.Module):
         q = self.q(feat).view(B, N, H, d).permute(0, 2, 1, 3).contiguous()
         kv = self.kv(feat).view(B, N, H, 2 * d).permute(0, 2, 1, 3)
         k, v = kv[..., :d].contiguous(), kv[..., d:].contiguous()
-        bias = pos_bias_gather(self.pos_embed(self.rel_table), pe_idx)     # [B,H,N,M]
+        bias = rel_pos_bias(self.pos_embed.weight, self.pos_embed.bias, pe_idx, q.dtype)  # [B,H,N,M]
         out = FlashLocalAttentionFunction.apply(
             q, k, v, member_idx, bias, None if mask is None else mask[:, None],
             self.blank_k.view(H, d), self.blank_v.view(H, d), float(self.scale))

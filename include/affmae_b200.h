@@ -107,6 +107,19 @@ int affb_pos_bias_bwd(const void* dbias, const int64_t* pe_idx, int dtype, int64
                       int64_t H, int64_t B, int64_t N, int64_t M, float* dtable_acc,
                       void* stream);
 
+/* Relative-position bias evaluated in the kernel (no table): replaces
+ * Linear(5 -> H)(pre_table) followed by the gather of _make_pos_bias
+ * (src/layers/attention.py:111-124; pre_table of src/utils/pos_embed.py:8-22).
+ * out[b,h,n,m] = weight[h,:] . f(pe_idx[b,n,m]) + bias[h] with
+ * f(i) = (dx, dy, r, dy/r, dx/r), dx = i % 255 - 127, dy = i / 255 - 127
+ * (last three 0 at r = 0).  weight [H,5] fp32, bias [H] fp32, pe_idx
+ * [B,N,M] int64 in [0, 65025), out [B,H,N,M] T, H <= 32.                   */
+int affb_rel_bias_fwd(const float* weight, const float* bias, const int64_t* pe_idx, int dtype,
+                      int64_t H, int64_t B, int64_t N, int64_t M, void* out, void* stream);
+/* dweight [H,5], dbias_vec [H]: fp32 accumulators zeroed by the caller.    */
+int affb_rel_bias_bwd(const void* dbias, const int64_t* pe_idx, int dtype, int64_t H, int64_t B,
+                      int64_t N, int64_t M, float* dweight, float* dbias_vec, void* stream);
+
 /* --------------------------------- fused KNN deformable attention (2-D) --
  * Replaces fused_knn_deform_cross_attn_forward_save
  * (src/layers/kernels/fused_deform_attn.py:2592) and, with kv_pos == query_pos

@@ -521,3 +521,28 @@ def test_local_attn_partial_last_cluster(cuda, dtype):
                                    inp["do"], **kw(inp))
         for name, a, b in zip(["dq", "dk", "dv", "dbias", "dbk", "dbv"], grads, ref):
             assert rel_err(a.cpu(), b) < TOL_LP, (variant, name)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rel_pos_bias_matches_table_gather(cuda, dtype):
+    """In-kernel relative-position bias == Linear(5 -> H) over the reference's
+    table followed by the gather; weight/bias gradients == autograd of that."""
+    from affmae_b200.kernels.pos_bias import rel_pos_bias
+    from affmae_b200.workloads import relative_position_table
+    g = torch.Generator().manual_seed(3)
+    H, B, N, M = 6, 2, 97, 48
+    w = (torch.randn((H, 5), generator=g) * 0.3).to(cuda).requires_grad_(True)
+    b = (torch.randn((H,), generator=g) * 0.1).to(cuda).requires_grad_(True)
+    # offsets within +-20 tokens plus a few at the clamp limits and zero
+    pe = (torch.randint(107, 148, (B, N, M), generator=g) * 255 + torch.randint(107, 148, (B, N, M), generator=g))
+    pe[0, 0, :3] = torch.tensor([0, 65024, 127 * 255 + 127])
+    pe = pe.to(cuda)
+    out = rel_pos_bias(w, b, pe, dtype)
+    table = relative_position_table().to(cuda)
+    ref = (table @ w.T + b)[pe].permute(0, 3, 1, 2)
+    assert rel_err(out.float().cpu(), ref.detach().cpu()) < (1e-6 if dtype == torch.float32 else 8e-3)
+    go = torch.randn(ref.shape, generator=g).to(cuda)
+    gw, gb = torch.autograd.grad(out, (w, b), go.to(dtype))
+    rw, rb = torch.autograd.grad(ref, (w, b), go.to(dtype).float())
+    assert rel_err(gw.cpu(), rw.cpu()) < 1e-4 and rel_err(gb.cpu(), rb.cpu()) < 1e-4

@@ -24,6 +24,7 @@ _p = C.c_void_p
 _i64 = C.c_int64
 _i32 = C.c_int
 _f32 = C.c_float
+_u32 = C.c_uint32
 
 # entry point -> argtypes (all return an int status)
 SIGNATURES = {
@@ -37,6 +38,10 @@ SIGNATURES = {
                            _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "affb_pos_bias_fwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "affb_rel_bias_fwd": [_p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p],
+    "affb_layer_norm_fwd": [_p, _i32, _p, _i32, _f32, _u32, _p, _p, _f32, _i64, _i64, _p, _p, _p, _p, _p,
+                            _p],
+    "affb_layer_norm_bwd": [_p, _p, _p, _i32, _p, _p, _p, _f32, _u32, _i64, _i64, _p, _p, _i32, _p, _p,
+                            _p],
     "affb_rel_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p],
     "affb_pos_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "affb_deform_knn_fwd": [_p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p,

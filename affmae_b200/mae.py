@@ -17,7 +17,9 @@ on its path runs on this package's CUDA kernels:
   * the decoder's deformable self/cross attention runs on the fused
     KNN-Shepard deformable kernels.
 
-Dense layers (Linear, LayerNorm, GELU, convolutions) are PyTorch modules.
+Dense layers (Linear, GELU, convolutions) are PyTorch modules; the
+LayerNorms of the encoder blocks, stage outputs, merging and decoder blocks
+run on the fused residual + dropout + LayerNorm kernels.
 Deliberate differences from the reference: tokens are masked with uniform
 random noise (the reference's Perlin-noise masking depends on the
 ``perlin_noise`` package), and the unused ``global_norm`` / ``global_linear``
@@ -36,6 +38,7 @@ import torch.nn.functional as F
 from .kernels.fused_deform_attn import (fused_knn_deformable_cross_attention,
                                         fused_knn_deformable_self_attention)
 from .kernels.knn import knn
+from .kernels.layer_norm import FusedLayerNorm
 from .kernels.local_attn import FlashLocalAttentionFunction
 from .kernels.pos_bias import pos_bias_gather, rel_pos_bias
 from .kernels.weighted_features import weighted_features
@@ -91,12 +94,14 @@ def curve_clusters(pos: torch.Tensor, m: int, h: int, w: int):
     visit = gy * nx + torch.where(gy % 2 == 1, nx - 1 - gx, gx)          # visiting rank of each cell
     cell_xy = torch.empty((ny * nx, 2), device=dev)
     cell_xy[visit.reshape(-1)] = torch.stack([gx, gy], -1).reshape(-1, 2).float()
-    size = torch.tensor([cx, cy], device=dev)
-    anchors = cell_xy * size + size / 2 - 0.5                            # anchor centres in visiting order
+    # cell sizes as fp32 scalars (no host-to-device copy, so nothing waits for the GPU)
+    sx, sy = float(torch.tensor(cx, dtype=torch.float32)), float(torch.tensor(cy, dtype=torch.float32))
+    anchors = torch.stack([cell_xy[:, 0] * sx + sx / 2 - 0.5, cell_xy[:, 1] * sy + sy / 2 - 0.5], -1)
     prev = torch.cat([2 * anchors[:1] - anchors[1:2], anchors[:-1]], 0)
     nxt = torch.cat([anchors[1:], 2 * anchors[-1:] - anchors[-2:-1]], 0)
-    c = (pos / size).floor().long()
-    rank = visit.reshape(-1)[c[..., 0] + c[..., 1] * nx]                 # [B,n]
+    fx = (pos[..., 0] / sx).floor().long()
+    fy = (pos[..., 1] / sy).floor().long()
+    rank = visit.reshape(-1)[fx + fy * nx]                               # [B,n]
     d_prev = (pos - prev[rank]).pow(2).sum(-1)
     d_next = (pos - nxt[rank]).pow(2).sum(-1)
     ratio = d_prev / (d_next + 1e-5)
@@ -176,17 +181,20 @@ class ClusterAttention(nn.Module):
 class ClusterBlock(nn.Module):
     def __init__(self, dim: int, heads: int, mlp_ratio: float, drop_path: float):
         super().__init__()
-        self.norm1 = nn.LayerNorm(dim)
+        self.norm1 = FusedLayerNorm(dim)
         self.attn = ClusterAttention(dim, heads)
-        self.norm2 = nn.LayerNorm(dim)
+        self.norm2 = FusedLayerNorm(dim)
         hidden = int(dim * mlp_ratio)
         self.fc1 = nn.Linear(dim, hidden)
         self.fc2 = nn.Linear(hidden, dim)
         self.drop_path = DropPath(drop_path)
 
     def forward(self, feat, member_idx, mask, pe_idx):
-        feat = feat + self.drop_path(self.attn(self.norm1(feat), member_idx, mask, pe_idx))
-        return feat + self.drop_path(self.fc2(F.gelu(self.fc1(self.norm2(feat)))))
+        # pre-norms feed only Linears: produced directly in the autocast dtype
+        h = self.norm1(feat, out32=False, out16=True)
+        feat = feat + self.drop_path(self.attn(h, member_idx, mask, pe_idx))
+        h = self.norm2(feat, out32=False, out16=True)
+        return feat + self.drop_path(self.fc2(F.gelu(self.fc1(h))))
 
 
 class ClusterMerging(nn.Module):
@@ -199,7 +207,7 @@ class ClusterMerging(nn.Module):
         super().__init__()
         self.ds_rate = ds_rate
         self.weight_net = nn.Sequential(nn.Linear(5, inner), nn.LayerNorm(inner), nn.GELU())
-        self.norm = nn.LayerNorm(inner * dim)
+        self.norm = FusedLayerNorm(inner * dim)
         self.linear = nn.Linear(inner * dim, out_dim)
         self.register_buffer("rel_table", relative_position_table(), persistent=False)
 
@@ -220,7 +228,7 @@ class ClusterMerging(nn.Module):
         # block-reduced scatter-add into the table instead of a sorted index_put
         weights = pos_bias_gather(table, pe).permute(0, 2, 3, 1) * lp     # [B,keep,M,inner]
         merged = weighted_features(weights.to(feat.dtype), feat, member)  # [B,keep,inner,C]
-        return pos_down, self.linear(self.norm(merged.reshape(B, keep, -1)))
+        return pos_down, self.linear(self.norm(merged.reshape(B, keep, -1), out32=False, out16=True))
 
 
 class Stage(nn.Module):
@@ -296,7 +304,7 @@ class Encoder(nn.Module):
             out = cfg.embed_dims[i + 1] if i + 1 < len(cfg.depths) else None
             s0 = sum(cfg.depths[:i])
             self.stages.append(Stage(cfg.embed_dims[i], out, depth, cfg.num_heads[i], cfg, dpr[s0:s0 + depth]))
-        self.norms = nn.ModuleList(nn.LayerNorm(d) for d in cfg.embed_dims)
+        self.norms = nn.ModuleList(FusedLayerNorm(d) for d in cfg.embed_dims)
         self._init()
 
     def _init(self):
@@ -327,7 +335,7 @@ class Encoder(nn.Module):
         outs = []
         for stage, norm in zip(self.stages, self.norms):
             pos_out, x_out, pos, feat = stage(pos, feat, h, w)
-            outs.append((norm(x_out), pos_out))
+            outs.append((norm(x_out, out32=False, out16=True), pos_out))  # consumed by Linears only
         return outs
 
 
@@ -399,15 +407,21 @@ class DecoderBlock(nn.Module):
         super().__init__()
         self.self_attn = DeformableAttention(dim, heads)
         self.cross_attn = DeformableAttention(dim, heads)
-        self.norm1, self.norm2, self.norm3 = nn.LayerNorm(dim), nn.LayerNorm(dim), nn.LayerNorm(dim)
+        self.norm1, self.norm2, self.norm3 = FusedLayerNorm(dim), FusedLayerNorm(dim), FusedLayerNorm(dim)
         self.linear1 = nn.Linear(dim, ffn)
         self.linear2 = nn.Linear(ffn, dim)
+        self.p = dropout
         self.drop = nn.Dropout(dropout)
 
-    def forward(self, q, q_pos, src, src_pos, src_embed):
-        q = self.norm1(q + self.drop(self.self_attn(q, q_pos)))
-        q = self.norm2(q + self.drop(self.cross_attn(q, q_pos, src + src_embed, src_pos)))
-        return self.norm3(q + self.drop(self.linear2(self.drop(F.relu(self.linear1(q))))))
+    def forward(self, q, q16, q_pos, src, src_pos, src_embed):
+        """q: fp32 residual stream; q16: the same values in the autocast dtype
+        (the Linears' input).  Each norm(q + dropout(delta)) is one fused pass
+        returning both."""
+        q, q16 = self.norm1(q, self.self_attn(q16, q_pos), self.p, out32=True, out16=True)
+        q, q16 = self.norm2(q, self.cross_attn(q16, q_pos, src + src_embed, src_pos), self.p,
+                            out32=True, out16=True)
+        ff = self.linear2(self.drop(F.relu(self.linear1(q16))))
+        return self.norm3(q, ff, self.p, out32=True, out16=True)
 
 
 class PixelDecoder(nn.Module):
@@ -429,10 +443,11 @@ class PixelDecoder(nn.Module):
 
     def forward(self, stages, queries, q_pos):
         q = queries + sine_embedding(q_pos, self.dim).to(queries.dtype)
+        q16 = q
         outs = []
         for proj, blk, (feat, pos) in zip(self.input_proj, self.blocks, reversed(stages)):
             src = proj(feat)
-            q = blk(q, q_pos, src, pos, sine_embedding(pos, self.dim).to(src.dtype))
+            q, q16 = blk(q, q16, q_pos, src, pos, sine_embedding(pos, self.dim).to(src.dtype))
             outs.append(q)
         return outs  # coarsest level first
 

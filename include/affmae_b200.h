@@ -120,6 +120,26 @@ int affb_rel_bias_fwd(const float* weight, const float* bias, const int64_t* pe_
 int affb_rel_bias_bwd(const void* dbias, const int64_t* pe_idx, int dtype, int64_t H, int64_t B,
                       int64_t N, int64_t M, float* dweight, float* dbias_vec, void* stream);
 
+/* ------------------------------- fused residual + dropout + LayerNorm --
+ * The add / dropout / LayerNorm / dtype-cast sequences around the operators
+ * above in the model (decoder blocks, src/layers/decoder.py:114-143, and the
+ * encoder pre-norms, src/layers/aff.py:95-115) as one pass per direction.
+ * Forward: s = x + dropout_p(delta) (delta may be NULL), y = LN(s) written to
+ * y32 (fp32) and/or y16_bf16; rows R of C <= 1536 channels; x and delta fp32
+ * or bf16; s_saved [R,C] fp32 (needed with delta), mean/rstd [R] fp32.  The
+ * dropout mask is a hash of (seed, element index).                          */
+int affb_layer_norm_fwd(const void* x, int x_dtype, const void* delta, int delta_dtype, float p,
+                        uint32_t seed, const float* gamma, const float* beta, float eps, int64_t R,
+                        int64_t C, float* s_saved, float* mean, float* rstd, float* y32,
+                        void* y16_bf16, void* stream);
+/* Backward: dy32 and/or dy16_bf16 summed; s = s_saved (fp32) or x (s_dtype);
+ * dx written in s_dtype, ddelta (NULL when the forward had no delta) in
+ * delta_dtype; dgamma, dbeta [C] fp32 accumulators zeroed by the caller.    */
+int affb_layer_norm_bwd(const float* dy32, const void* dy16_bf16, const void* s, int s_dtype,
+                        const float* mean, const float* rstd, const float* gamma, float p,
+                        uint32_t seed, int64_t R, int64_t C, void* dx, void* ddelta,
+                        int delta_dtype, float* dgamma, float* dbeta, void* stream);
+
 /* --------------------------------- fused KNN deformable attention (2-D) --
  * Replaces fused_knn_deform_cross_attn_forward_save
  * (src/layers/kernels/fused_deform_attn.py:2592) and, with kv_pos == query_pos

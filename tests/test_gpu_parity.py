@@ -546,3 +546,57 @@ def test_rel_pos_bias_matches_table_gather(cuda, dtype):
     gw, gb = torch.autograd.grad(out, (w, b), go.to(dtype))
     rw, rb = torch.autograd.grad(ref, (w, b), go.to(dtype).float())
     assert rel_err(gw.cpu(), rw.cpu()) < 1e-4 and rel_err(gb.cpu(), rb.cpu()) < 1e-4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("C", [48, 96, 384, 1536])
+def test_fused_layer_norm_matches_torch(cuda, xdtype, C):
+    """LayerNorm(x) with fp32 and bf16 outputs, values and all gradients, against
+    torch.nn.functional.layer_norm in fp32."""
+    from affmae_b200.kernels.layer_norm import fused_layer_norm
+    g = torch.Generator().manual_seed(C)
+    x = (torch.randn((3, 77, C), generator=g) * 2 + 0.5).to(cuda, xdtype).requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(C, generator=g)).to(cuda).requires_grad_(True)
+    b = (0.1 * torch.randn(C, generator=g)).to(cuda).requires_grad_(True)
+    y32, y16 = fused_layer_norm(x, w, b, 1e-5, out32=True, out16=True)
+    xr = x.detach().float().requires_grad_(True)
+    ref = torch.nn.functional.layer_norm(xr, (C,), w, b, 1e-5)
+    assert rel_err(y32.cpu(), ref.detach().cpu()) < 1e-5
+    assert rel_err(y16.float().cpu(), ref.detach().cpu()) < 8e-3
+    g32 = torch.randn(ref.shape, generator=g).to(cuda)
+    g16 = torch.randn(ref.shape, generator=g).to(cuda, torch.bfloat16)
+    dx, dw, db = torch.autograd.grad((y32, y16), (x, w, b), (g32, g16))
+    rx, rw, rb = torch.autograd.grad(ref, (xr, w, b), g32 + g16.float())
+    tol = 1e-4 if xdtype == torch.float32 else 8e-3
+    assert rel_err(dx.float().cpu(), rx.cpu()) < tol
+    assert rel_err(dw.cpu(), rw.cpu()) < 1e-4 and rel_err(db.cpu(), rb.cpu()) < 1e-4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("p", [0.0, 0.1])
+def test_fused_residual_dropout_layer_norm(cuda, p):
+    """LayerNorm(x + dropout(delta)) with a bf16 delta: without dropout equal to
+    the torch sequence; with dropout the mask seen by the backward (zeros of
+    d_delta) is the one the forward applied, and about p of the elements drop."""
+    from affmae_b200.kernels.layer_norm import fused_layer_norm
+    g = torch.Generator().manual_seed(5)
+    C = 384
+    x = torch.randn((4, 300, C), generator=g).to(cuda).requires_grad_(True)
+    d = torch.randn((4, 300, C), generator=g).to(cuda, torch.bfloat16).requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(C, generator=g)).to(cuda).requires_grad_(True)
+    b = (0.1 * torch.randn(C, generator=g)).to(cuda).requires_grad_(True)
+    y32 = fused_layer_norm(x, w, b, 1e-5, delta=d, p=p, out32=True)
+    gy = torch.randn(y32.shape, generator=g).to(cuda)
+    dx, dd = torch.autograd.grad(y32, (x, d), gy)
+    keep = (dd != 0).float() if p > 0 else torch.ones_like(x)
+    if p > 0:
+        frac = 1 - keep.mean().item()
+        assert abs(frac - p) < 0.01, frac
+    xr = x.detach().clone().requires_grad_(True)
+    dr = d.detach().float().clone().requires_grad_(True)
+    ref = torch.nn.functional.layer_norm(xr + dr * keep / (1 - p), (C,), w, b, 1e-5)
+    assert rel_err(y32.cpu(), ref.detach().cpu()) < 1e-5
+    rx, rd = torch.autograd.grad(ref, (xr, dr), gy)
+    assert rel_err(dx.cpu(), rx.cpu()) < 1e-4
+    assert rel_err(dd.float().cpu(), rd.cpu()) < 8e-3

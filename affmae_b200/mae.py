@@ -433,7 +433,7 @@ class PixelDecoder(nn.Module):
         super().__init__()
         D = cfg.decoder_dim
         self.dim = D
-        self.input_proj = nn.ModuleList(nn.Sequential(nn.Linear(c, D), nn.LayerNorm(D))
+        self.input_proj = nn.ModuleList(nn.Sequential(nn.Linear(c, D), FusedLayerNorm(D))
                                         for c in reversed(cfg.embed_dims))
         for proj in self.input_proj:
             nn.init.xavier_uniform_(proj[0].weight)
@@ -454,6 +454,18 @@ class PixelDecoder(nn.Module):
 
 # ------------------------------------------------------------------- model --
 
+class PredictionHead(nn.Module):
+    """LayerNorm + Linear to the patch pixels (reference aff_mae.py:80-92)."""
+
+    def __init__(self, dim: int, out: int):
+        super().__init__()
+        self.norm = FusedLayerNorm(dim)
+        self.linear = nn.Linear(dim, out)
+
+    def forward(self, x):
+        return self.linear(self.norm(x, out32=False, out16=True))
+
+
 class AFFMaskedAutoEncoder(nn.Module):
     """forward(images [B,C,H,W]) -> (loss, [loss_res5, loss_res4, loss_res2])."""
 
@@ -465,9 +477,9 @@ class AFFMaskedAutoEncoder(nn.Module):
         D = cfg.decoder_dim
         out = cfg.patch_size ** 2 * cfg.in_chans
         self.masked_token = nn.Parameter(torch.randn(1, 1, D) * 0.02)
-        self.head_res5 = nn.Sequential(nn.LayerNorm(D), nn.Linear(D, out))
-        self.head_res4 = nn.Sequential(nn.LayerNorm(D), nn.Linear(D, out))
-        self.head_res2 = nn.Sequential(nn.LayerNorm(D), nn.Linear(D, out))
+        self.head_res5 = PredictionHead(D, out)
+        self.head_res4 = PredictionHead(D, out)
+        self.head_res2 = PredictionHead(D, out)
 
     def patchify(self, imgs):
         p, c = self.cfg.patch_size, self.cfg.in_chans

@@ -254,6 +254,14 @@ deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
   }
 }
 
+// Backward, one warp per query.  Per head the 4 points x 4 neighbours give 16
+// (kv row, coefficient aw * w) entries; entries naming the same kv row are
+// merged first (neighbouring sampling points share neighbours), so each
+// distinct row is gathered once for the dot products and receives one
+// scatter-add of d_values.  The per-entry dot products v[row] . dout[head]
+// are reduced over the head's lanes with shuffles when a head's 8-channel
+// chunks form an aligned lane group (C/8 divides 32), else with shared-memory
+// atomics.
 template <typename T>
 __global__ void __launch_bounds__(DK_WARPS * 32)
 deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ kvpos,
@@ -265,15 +273,19 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
                       float* __restrict__ d_qpos, float* __restrict__ d_kvpos,
                       float* __restrict__ d_val, float* __restrict__ d_power) {
   __shared__ int s_idx[DK_WARPS][DK_SMAX * 4];
+  __shared__ int s_first[DK_WARPS][DK_SMAX * 4];   // first entry of the head with the same kv row
   __shared__ float s_w[DK_WARPS][DK_SMAX * 4];
-  __shared__ float s_dot[DK_WARPS][DK_SMAX * 4];
+  __shared__ float s_cf[DK_WARPS][DK_SMAX * 4];    // merged aw * w of a first entry
+  __shared__ float s_dot[DK_WARPS][DK_SMAX * 4];   // v[row] . dout[head] of a first entry
   __shared__ float s_aw[DK_WARPS][DK_SMAX];
-  __shared__ float s_datt[DK_WARPS][DK_SMAX];
   __shared__ float s_pow[DK_WARPS];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float P = fmaxf(power[0], 1e-6f);
   const int S = H * 4;
   const int row = H * C;
+  const int nc8 = row / 8;
+  const int G = C / 8;  // lanes (8-channel chunks) per head
+  const bool shfl = G <= 32 && (32 % G) == 0;
   float dpow = 0.f;
   for (int64_t gq = (int64_t)blockIdx.x * DK_WARPS + warp; gq < B * Nq;
        gq += (int64_t)gridDim.x * DK_WARPS) {
@@ -288,39 +300,53 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       s_idx[warp][s * 4 + 0] = ii.x; s_idx[warp][s * 4 + 1] = ii.y;
       s_idx[warp][s * 4 + 2] = ii.z; s_idx[warp][s * 4 + 3] = ii.w;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { s_w[warp][s * 4 + j] = w[j]; s_dot[warp][s * 4 + j] = 0.f; }
+      for (int j = 0; j < 4; ++j) { s_w[warp][s * 4 + j] = w[j]; s_cf[warp][s * 4 + j] = 0.f; s_dot[warp][s * 4 + j] = 0.f; }
       s_aw[warp][s] = attn_w[gs];
-      s_datt[warp][s] = 0.f;
+    }
+    __syncwarp();
+    // merge entries of a head that name the same kv row
+    for (int t = lane; t < S * 4; t += 32) {
+      const int h0 = (t >> 4) << 4, id = s_idx[warp][t];
+      int f = t;
+      for (int u = h0; u < t; ++u)
+        if (s_idx[warp][u] == id) { f = u; break; }
+      s_first[warp][t] = f;
+      atomicAdd(&s_cf[warp][f], s_aw[warp][t >> 2] * s_w[warp][t]);
     }
     __syncwarp();
     const T* vb = values + b * Nkv * row;
     float* dvb = d_val + b * Nkv * row;
-    for (int c8 = lane; c8 * 8 < row; c8 += 32) {
-      const int h = (c8 * 8) / C;
+    for (int base = 0; base < nc8; base += 32) {
+      const int c8 = base + lane;
+      const bool act = c8 < nc8;
+      const int h = act ? (c8 * 8) / C : 0;
       float g[8];
-      ld8(dout + gq * row + c8 * 8, g);
+      if (act) ld8(dout + gq * row + c8 * 8, g);
+      else {
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int si = h * 4 + p;
-        const float aw = s_aw[warp][si];
-        float datt = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int id = s_idx[warp][si * 4 + j];
-          const float w = s_w[warp][si * 4 + j];
+        for (int e = 0; e < 8; ++e) g[e] = 0.f;
+      }
+      for (int k = 0; k < 16; ++k) {
+        const int t = h * 16 + k;
+        const bool first = act && s_first[warp][t] == t;
+        float dot = 0.f;
+        if (first) {
+          const int id = s_idx[warp][t];
           float v[8];
           ld8(vb + (int64_t)id * row + c8 * 8, v);
-          float dot = 0.f;
 #pragma unroll
           for (int e = 0; e < 8; ++e) dot = fmaf(v[e], g[e], dot);
-          atomicAdd(&s_dot[warp][si * 4 + j], dot);
-          datt = fmaf(w, dot, datt);
-          const float cf = aw * w;
+          const float cf = s_cf[warp][t];
           float* dst = dvb + (int64_t)id * row + c8 * 8;
           red_add_v4(dst, cf * g[0], cf * g[1], cf * g[2], cf * g[3]);
           red_add_v4(dst + 4, cf * g[4], cf * g[5], cf * g[6], cf * g[7]);
         }
-        atomicAdd(&s_datt[warp][si], datt);
+        if (shfl) {
+          for (int o = G >> 1; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (first && (lane % G) == 0) s_dot[warp][t] = dot;
+        } else if (first) {
+          atomicAdd(&s_dot[warp][t], dot);
+        }
       }
     }
     __syncwarp();
@@ -336,11 +362,17 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       const float d2[4] = {dd.x, dd.y, dd.z, dd.w};
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
-      d_aw[gs] = s_datt[warp][s];
       const float aw = s_aw[warp][s];
+      float dot[4], datt = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dot[j] = s_dot[warp][s_first[warp][s * 4 + j]];
+        datt = fmaf(w[j], dot[j], datt);
+      }
+      d_aw[gs] = datt;
       float dp[4], wdp = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { dp[j] = aw * s_dot[warp][s * 4 + j]; wdp = fmaf(w[j], dp[j], wdp); }
+      for (int j = 0; j < 4; ++j) { dp[j] = aw * dot[j]; wdp = fmaf(w[j], dp[j], wdp); }
       float dsx = 0.f, dsy = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {

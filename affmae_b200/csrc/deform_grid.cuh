@@ -26,10 +26,13 @@ struct GridView {
   int64_t Nkv;
 };
 
-// Grid side: about two points per cell.
+// Grid side: about AFFB_GRID_PPC points per cell.
+#ifndef AFFB_GRID_PPC
+#define AFFB_GRID_PPC 4
+#endif
 __host__ __device__ inline int grid_side(int64_t nkv) {
   int64_t g = 1;
-  while (g * g * 2 < nkv && g < 4096) ++g;
+  while (g * g * AFFB_GRID_PPC < nkv && g < 4096) ++g;
   return (int)g;
 }
 

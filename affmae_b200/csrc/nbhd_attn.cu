@@ -155,8 +155,9 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
   cudaStream_t st = as_stream(stream);
   const int64_t nel = B * H * N * D;
   if (nbhd_tc_supported(dtype, D, M)) {
-    // lists -> prologue (D, blank terms) -> [query side, only for lists that
-    // are not all cluster runs] -> key side (dK, dV, dS) -> dQ from dS
+    // list count + prologue (D, blank terms) -> scan -> fill -> [query side,
+    // only for lists that are not all cluster runs] -> key side (dK, dV, dS)
+    // -> dQ from dS
     AFFB_REQUIRE(N * M < (1ll << 31), "nbhd_attn_bwd: N * M must be below 2^31 on the tensor-core path");
     a.dk = ly.acc_k; a.dv = ly.acc_v;
     a.general = ly.flag;
@@ -167,9 +168,11 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
     kv.dk = dk; kv.dv = dv;
     kv.Cc = (int)((N + 7) / 8);
     a.ds = kv.ds; a.dsb = ly.dsb;
-    if (int e = nbhd_inv_lists(a, kv, ly, (int)B, st)) return e;
-    if (int e = nbhd_q_prologue(a, kv, dtype, (int)B, st)) return e;
-    if (int e = nbhd_blk_bwd(a, dtype, (int)B, st)) return e;
+    if (int e = nbhd_bwd_prepare(a, kv, ly, dtype, (int)B, st)) return e;
+    NbhdArgs ag = a;  // the query-side kernel leaves the blank gradients to the prologue
+    ag.dbk = nullptr;
+    ag.dbv = nullptr;
+    if (int e = nbhd_blk_bwd(ag, dtype, (int)B, st)) return e;
     if (int e = nbhd_kv_bwd(a, kv, dtype, (int)B, st)) return e;
     if (int e = nbhd_blk_dq(a, dtype, (int)B, st)) return e;
   } else {

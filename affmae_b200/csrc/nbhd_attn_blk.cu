@@ -438,8 +438,10 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpBw
       gk = fmaf(ds_r, io<T>::ld(w.Q + swz(row, lane >> 3) + (lane & 7)), gk);
       gv = fmaf(pb_r, io<T>::ld(w.dO + swz(row, lane >> 3) + (lane & 7)), gv);
     }
-    red_add(a.dbk + (int64_t)h * TD + lane, gk * a.scale);
-    red_add(a.dbv + (int64_t)h * TD + lane, gv);
+    if (a.dbk) {  // null: the blank gradients are summed by the prologue kernel
+      red_add(a.dbk + (int64_t)h * TD + lane, gk * a.scale);
+      red_add(a.dbv + (int64_t)h * TD + lane, gv);
+    }
   }
   T* dbase = a.dbias ? (T*)a.dbias + (bh * N + n0) * M : nullptr;
   float qacc[4][4];
@@ -519,7 +521,8 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel
     if (nclu < 0) {  // not cluster-block lists: CUDA-core rows, blank-token grads straight to global
       for (int w = warp; w < a.H * nq; w += NW) {
         const int h = w / nq;
-        nbhd_bwd_row<T, 4>(a, b, h, n0 + w % nq, a.dbk + (int64_t)h * TD, a.dbv + (int64_t)h * TD);
+        nbhd_bwd_row<T, 4>(a, b, h, n0 + w % nq, a.dbk ? a.dbk + (int64_t)h * TD : nullptr,
+                           a.dbk ? a.dbv + (int64_t)h * TD : nullptr);
       }
       continue;
     }

@@ -5,7 +5,7 @@
 // The reference accumulates dK / dV by atomically adding each query's
 // contribution into fp32 buffers (local_attn.py:518-519, tl.atomic_add on
 // DK / DV).  Here the lists are inverted once per call instead:
-//   inv_count  one thread per query: checks that its list is M/8 runs of 8
+//   inv_count  one thread per query (sharing one launch with the prologue): checks that its list is M/8 runs of 8
 //              consecutive keys starting at a multiple of 8 with no cluster
 //              listed twice, where a run of the partial last cluster may end
 //              in padding slots masked in every mask head (the same test as
@@ -49,11 +49,11 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid
 
 // ---------------------------------------------------------------- lists --
 
-__global__ void nbhd_inv_count_kernel(const int32_t* __restrict__ midx, const uint8_t* __restrict__ mask,
-                                      int mask_heads, int B, int N, int M, int Cc,
-                                      int* __restrict__ flag, int* __restrict__ counts,
-                                      int* __restrict__ ecl, int* __restrict__ erk) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void inv_count_block(const int32_t* __restrict__ midx, const uint8_t* __restrict__ mask,
+                                                int mask_heads, int B, int N, int M, int Cc,
+                                                int* __restrict__ flag, int* __restrict__ counts,
+                                                int* __restrict__ ecl, int* __restrict__ erk, int64_t bid) {
+  const int64_t t = bid * blockDim.x + threadIdx.x;
   const bool valid = t < (int64_t)B * N;
   const int b = valid ? (int)(t / N) : 0;
   const int64_t qn = valid ? t - (int64_t)b * N : 0;  // query index within its image
@@ -187,15 +187,14 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
 constexpr int PRO_ROWS = 256;
 
 template <typename T>
-__global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs k) {
+__device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs& k, int64_t bid) {
   __shared__ float s_dbk[TD], s_dbv[TD];
-  if (*k.flag) return;
   const int N = a.N;
   const int nblk = (N + PRO_ROWS - 1) / PRO_ROWS;
-  const int64_t bh = blockIdx.x / nblk;
+  const int64_t bh = bid / nblk;
   const int h = (int)(bh % a.H);
   const int t = threadIdx.x, lane = t & 31, sub = lane & 3;
-  const int nbase = (blockIdx.x % nblk) * PRO_ROWS;
+  const int nbase = (int)(bid % nblk) * PRO_ROWS;
   const bool blank = a.blank_k != nullptr;
   float bkv[8], bvv[8], gk[8], gv[8];
 #pragma unroll
@@ -210,8 +209,9 @@ __global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs
     const int n = nbase + r0 + (t >> 2);
     const bool valid = n < N;
     const int64_t row = bh * N + n;
-    float ov[8], dv[8], qv[8], di = 0.f;
+    float ov[8], dv[8], qv[8], di = 0.f, ls = 0.f;
     if (valid) {
+      if (blank) ls = __ldg(a.lse + row);  // issued with the row loads, used after the reductions
       ld8((const T*)a.o + row * TD + sub * 8, ov);
       ld8((const T*)a.dout + row * TD + sub * 8, dv);
       if (blank) ld8((const T*)a.q + row * TD + sub * 8, qv);
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs
         dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
       }
       if (valid) {
-        const float pb = expf(sb * a.scale - a.lse[row]);
+        const float pb = expf(sb * a.scale - ls);
         const float dsb = pb * (dpb - di);
         if (sub == 0) k.dsb[row] = dsb;
 #pragma unroll
@@ -265,14 +265,21 @@ __global__ void __launch_bounds__(256) nbhd_q_prologue_kernel(NbhdArgs a, KvArgs
   }
 }
 
-int nbhd_q_prologue(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st) {
-  const int64_t blocks = (int64_t)B * a.H * ((a.N + PRO_ROWS - 1) / PRO_ROWS);
-  if (blocks == 0) return AFFB_OK;
-  AFFB_REQUIRE(blocks < (1ll << 31), "nbhd_attn_bwd: too many rows");
-  if (dtype == AFFB_BF16) nbhd_q_prologue_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(a, k);
-  else nbhd_q_prologue_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(a, k);
-  return AFFB_OK;
+// The list count (one thread per query) and the prologue (rows of one (b, h))
+// share one launch: blocks [0, count_blocks) count, the rest run the prologue.
+// The prologue does not wait for the list check: D, the blank dS and the
+// blank-token gradients are the same whichever kernels do the rest.
+template <typename T>
+__global__ void __launch_bounds__(256) nbhd_bwd_pre_kernel(NbhdArgs a, KvArgs k, NbhdBwdLayout ly,
+                                                          int count_blocks, int B, int Cc) {
+  if (blockIdx.x < count_blocks) {
+    inv_count_block(a.midx, a.mask, a.mask_heads, B, a.N, a.M, Cc, ly.flag, ly.counts, ly.ecl, ly.erk,
+                    blockIdx.x);
+    return;
+  }
+  q_prologue_block<T>(a, k, blockIdx.x - count_blocks);
 }
+
 
 // ------------------------------------------------------ key-major pass --
 
@@ -538,19 +545,23 @@ int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream
   return go(nbhd_kv_kernel<__half>, sizeof(KvSmem<__half>));
 }
 
-int nbhd_inv_lists(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, int B, cudaStream_t st) {
+int nbhd_bwd_prepare(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, int dtype, int B,
+                     cudaStream_t st) {
   const int N = a.N, M = a.M, Cc = k.Cc;
   const int64_t rows = (int64_t)B * N;
   if (cudaMemsetAsync(ly.flag, 0, ly.zero_bytes, st) != cudaSuccess) {
     set_error("nbhd_attn_bwd: cudaMemsetAsync failed");
     return AFFB_ERR_CUDA;
   }
-  const unsigned g = (unsigned)((rows + 255) / 256);
-  nbhd_inv_count_kernel<<<g, 256, 0, st>>>(a.midx, a.mask, a.mask_heads, B, N, M, Cc, ly.flag, ly.counts,
-                                           ly.ecl, ly.erk);
+  const int64_t cnt = (rows + 255) / 256;
+  const int64_t pro = (int64_t)B * a.H * ((N + PRO_ROWS - 1) / PRO_ROWS);
+  AFFB_REQUIRE(cnt + pro < (1ll << 31), "nbhd_attn_bwd: too many rows");
+  const unsigned g = (unsigned)(cnt + pro);
+  if (dtype == AFFB_BF16) nbhd_bwd_pre_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(a, k, ly, (int)cnt, B, Cc);
+  else nbhd_bwd_pre_kernel<__half><<<g, 256, 0, st>>>(a, k, ly, (int)cnt, B, Cc);
   nbhd_inv_scan_kernel<<<B, 1024, 0, st>>>(ly.counts, N, M >> 3, Cc, ly.flag, ly.offs);
-  nbhd_inv_fill_kernel<<<g, 256, 0, st>>>(B, N, M, Cc, a.H, ly.flag, ly.offs, ly.ecl, ly.erk, ly.entries,
-                                          ly.acc_k, ly.acc_v);
+  nbhd_inv_fill_kernel<<<(unsigned)cnt, 256, 0, st>>>(B, N, M, Cc, a.H, ly.flag, ly.offs, ly.ecl, ly.erk,
+                                                     ly.entries, ly.acc_k, ly.acc_v);
   return AFFB_OK;
 }
 

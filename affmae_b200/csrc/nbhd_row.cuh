@@ -250,7 +250,7 @@ __device__ void nbhd_bwd_row(const NbhdArgs& a, int b, int h, int n, float* dbk_
     const float dsb = pb * (dpb - delta);
 #pragma unroll
     for (int e = 0; e < 8; ++e) dqa[e] = fmaf(dsb, bk[e], dqa[e]);
-    if (g == 0 && dvalid) {
+    if (g == 0 && dvalid && dbk_acc) {  // null: the blank gradients are summed elsewhere
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         atomicAdd(&dbk_acc[ch * 8 + e], a.scale * dsb * qv[e]);

@@ -86,8 +86,9 @@ int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 // Key side (nbhd_attn_kv.cu).
-int nbhd_inv_lists(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, int B, cudaStream_t st);
-int nbhd_q_prologue(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st);
+// flag + counts cleared, list count and prologue (one launch), scan, fill
+int nbhd_bwd_prepare(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly, int dtype, int B,
+                     cudaStream_t st);
 int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream_t st);
 
 }  // namespace affb

@@ -279,7 +279,9 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpFw
     sbv[0] *= a.scale;
     sbv[1] *= a.scale;
   }
-  float m[2] = {-1e11f, -1e11f}, l[2] = {0.f, 0.f};
+  // running max m per row (natural units) and m * log2(e), the offset of the
+  // base-2 exponentials p = 2^(s * log2(e) - m * log2(e))
+  float m[2] = {-1e11f, -1e11f}, m2[2] = {-1e11f * kLog2e, -1e11f * kLog2e}, l[2] = {0.f, 0.f};
   float o[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -299,29 +301,36 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpFw
         const int row = g + hf * 8;
         float b0, b1;
         bias_at(w.bias, s.boff[row][2 * c + nt], tq, b0, b1);
-        x[nt][2 * hf] = x[nt][2 * hf] * a.scale + b0;
-        x[nt][2 * hf + 1] = x[nt][2 * hf + 1] * a.scale + b1;
+        x[nt][2 * hf] = fmaf(x[nt][2 * hf], a.scale, b0);
+        x[nt][2 * hf + 1] = fmaf(x[nt][2 * hf + 1], a.scale, b1);
         cm[hf] = fmaxf(cm[hf], fmaxf(x[nt][2 * hf], x[nt][2 * hf + 1]));
       }
     }
-    float al[2];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       cm[hf] = fmaxf(cm[hf], __shfl_xor_sync(0xffffffffu, cm[hf], 1));
       cm[hf] = fmaxf(cm[hf], __shfl_xor_sync(0xffffffffu, cm[hf], 2));
-      const float nm = fmaxf(m[hf], cm[hf]);
-      al[hf] = __expf(m[hf] - nm);
-      m[hf] = nm;
-      l[hf] *= al[hf];
     }
+    // rescale O and l only when some row of the warp has a new maximum
+    if (__any_sync(0xffffffffu, cm[0] > m[0] || cm[1] > m[1])) {
+      float al[2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) { o[i][0] *= al[0]; o[i][1] *= al[0]; o[i][2] *= al[1]; o[i][3] *= al[1]; }
+      for (int hf = 0; hf < 2; ++hf) {
+        const float nm = fmaxf(m[hf], cm[hf]);
+        al[hf] = ex2_approx((m[hf] - nm) * kLog2e);
+        m[hf] = nm;
+        m2[hf] = nm * kLog2e;
+        l[hf] *= al[hf];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { o[i][0] *= al[0]; o[i][1] *= al[0]; o[i][2] *= al[1]; o[i][3] *= al[1]; }
+    }
     float p[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        p[nt][e] = __expf(x[nt][e] - m[e >> 1]);
+        p[nt][e] = ex2_approx(fmaf(x[nt][e], kLog2e, -m2[e >> 1]));
         l[e >> 1] += p[nt][e];
       }
     const uint32_t pa[4] = {pack2<T>(p[0][0], p[0][1]), pack2<T>(p[0][2], p[0][3]),

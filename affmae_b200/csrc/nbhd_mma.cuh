@@ -154,6 +154,15 @@ __device__ __forceinline__ void load_a_frags(uint32_t (*a)[4], const T* A) {
     ldsm_x4(a[ks], A + swz((lane & 7) + ((lane >> 3) & 1) * 8, ks * 2 + (lane >> 4)));
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x by the ex2.approx instruction (the base-2 exponential of the softmaxes).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T> __device__ __forceinline__ T neg_inf();
 template <> __device__ __forceinline__ __nv_bfloat16 neg_inf<__nv_bfloat16>() { return __ushort_as_bfloat16(0xFF80); }
 template <> __device__ __forceinline__ __half neg_inf<__half>() { return __ushort_as_half(0xFC00); }

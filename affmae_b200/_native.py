@@ -38,6 +38,7 @@ SIGNATURES = {
                            _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "affb_pos_bias_fwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "affb_rel_bias_fwd": [_p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p],
+    "affb_knn2d": [_p, _p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p],
     "affb_layer_norm_fwd": [_p, _i32, _p, _i32, _f32, _u32, _p, _p, _f32, _i64, _i64, _p, _p, _p, _p, _p,
                             _p],
     "affb_layer_norm_bwd": [_p, _p, _p, _i32, _p, _p, _p, _f32, _u32, _i64, _i64, _p, _p, _i32, _p, _p,
@@ -62,7 +63,8 @@ SIGNATURES = {
     "affb_cast_f32": [_p, _p, _i32, _i64, _p],
 }
 OTHER_SYMBOLS = ["affb_last_error", "affb_abi_version", "affb_deform_workspace_bytes",
-                 "affb_deform_noalloc_max_scratch_bytes", "affb_nbhd_attn_bwd_workspace_bytes"]
+                 "affb_deform_noalloc_max_scratch_bytes", "affb_nbhd_attn_bwd_workspace_bytes",
+                 "affb_knn2d_workspace_bytes"]
 
 
 def library_path() -> Path:
@@ -92,6 +94,8 @@ def lib():
         l.affb_deform_noalloc_max_scratch_bytes.argtypes = []
         l.affb_nbhd_attn_bwd_workspace_bytes.restype = C.c_int64
         l.affb_nbhd_attn_bwd_workspace_bytes.argtypes = [_i32, _i64, _i64, _i64, _i64, _i64]
+        l.affb_knn2d_workspace_bytes.restype = C.c_int64
+        l.affb_knn2d_workspace_bytes.argtypes = [_i64, _i64]
         for name, args in SIGNATURES.items():
             fn = getattr(l, name)
             fn.argtypes = args

@@ -92,6 +92,31 @@ __device__ __forceinline__ int cell_coord(float f, int G) {
   return (f >= 0.f) ? (f < (float)G ? (int)f : G - 1) : 0;
 }
 
+// Builds the grid of `nkv` points per batch element ([B, nkv, 2] fp32) in a
+// workspace of grid_layout(B, nkv).total bytes (deform_knn.cu).
+int build_grid(const float* pts, int64_t B, int64_t nkv, void* ws, GridView& gv, cudaStream_t st);
+
+// Lower bound of the distance from (sx, sy) to any point outside the cells
+// [x0, x1] x [y0, y1] (already visited), minus `slack`; `open` is false when
+// those cells cover the whole grid.
+__device__ __forceinline__ float outside_bound(const float* P, int G, int x0, int x1, int y0, int y1, float sx,
+                                               float sy, float slack, bool& open) {
+  const float minx = P[0], miny = P[1], cw = P[2], ch = P[3];
+  float lb = 3.4e38f;
+  open = false;
+  if (x0 > 0) { lb = fminf(lb, sx - (minx + x0 * cw)); open = true; }
+  if (x1 < G - 1) { lb = fminf(lb, (minx + (x1 + 1) * cw) - sx); open = true; }
+  if (y0 > 0) { lb = fminf(lb, sy - (miny + y0 * ch)); open = true; }
+  if (y1 < G - 1) { lb = fminf(lb, (miny + (y1 + 1) * ch) - sy); open = true; }
+  return lb - slack;
+}
+
+// Slack for the rounding of cell assignment and of boundary positions.
+__device__ __forceinline__ float grid_slack(const float* P, int G, float sx, float sy) {
+  const float cw = P[2], ch = P[3];
+  return 1e-4f * fmaxf(cw, ch) + 2e-6f * (fabsf(sx) + fabsf(sy) + fabsf(P[0]) + fabsf(P[1]) + G * fmaxf(cw, ch));
+}
+
 // Exact 4-NN of (sx, sy) among the points of batch element b.
 __device__ inline void grid_knn4(const GridView& g, int64_t b, float sx, float sy, Top4& top) {
   top.init();

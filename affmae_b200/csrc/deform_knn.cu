@@ -145,8 +145,7 @@ __global__ void grid_scatter_kernel(const float* __restrict__ pos, int64_t B, in
   }
 }
 
-static int build_grid(const float* kv_pos, int64_t B, int64_t nkv, void* ws, GridView& gv,
-                      cudaStream_t st) {
+int build_grid(const float* kv_pos, int64_t B, int64_t nkv, void* ws, GridView& gv, cudaStream_t st) {
   const GridLayout L = grid_layout(B, nkv);
   char* base = (char*)ws;
   float* params = (float*)(base + L.off_params);

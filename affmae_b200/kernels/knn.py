@@ -2,9 +2,11 @@
 
 Public API as in the reference: ``knn`` (knn.py:1615), ``knn_triton``
 (:1585), ``KNNFunction`` (:1543) and ``knn_forward`` (:1368).  One exact
-CUDA kernel serves every K (the reference switches to cdist+topk for K > 8):
-fp32 squared distances with separately rounded products and sums, ascending,
-ties broken by the lower index.
+rule serves every K (the reference switches to cdist+topk for K > 8): fp32
+squared distances with separately rounded products and sums, ascending, ties
+broken by the lower index.  Large 2-D searches (GRID_MIN_POINTS reference
+points, GRID_MIN_PAIRS query-point pairs) go through a uniform grid (same
+result as the brute-force scan, which serves 3-D / 4-D and small searches).
 """
 from __future__ import annotations
 
@@ -25,6 +27,11 @@ def _check(query, ref, k, D):
     assert k <= ref.shape[1], f"k={k} exceeds number of reference points N={ref.shape[1]}"
 
 
+GRID_MIN_POINTS = 128     # 2-D searches use the grid when the reference set has at least
+GRID_MIN_PAIRS = 1 << 21  # this many points and queries x points reaches this (else the
+                          # brute-force scan is cheaper than building the grid)
+
+
 def _knn_int64(query, ref, k, D):
     if query.dtype != ref.dtype or query.dtype not in (torch.float32, torch.float16, torch.bfloat16):
         query, ref = query.float(), ref.float()
@@ -33,6 +40,14 @@ def _knn_int64(query, ref, k, D):
     B, M, _ = query.shape
     N = ref.shape[1]
     out = torch.empty((B, M, k), dtype=torch.int64, device=query.device)
+    if D == 2 and N >= GRID_MIN_POINTS and M * N >= GRID_MIN_PAIRS:
+        # fp32 copies are exact for fp16 / bf16 points, so distances are unchanged
+        q32, r32 = nat.f32(query), nat.f32(ref)
+        wsb = int(nat.lib().affb_knn2d_workspace_bytes(B, N))
+        ws = torch.empty((wsb,), dtype=torch.uint8, device=query.device)
+        nat.call("affb_knn2d", nat.ptr(q32), nat.ptr(r32), B, M, N, int(k), nat.ptr(out), nat.ptr(ws), wsb,
+                 nat.stream(query.device))
+        return out
     nat.call("affb_knn", nat.ptr(query), nat.ptr(ref), nat.dcode(query), B, M, N, D, int(k),
              nat.ptr(out), nat.stream(query.device))
     return out

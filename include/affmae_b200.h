@@ -47,6 +47,12 @@ int affb_abi_version(void);
  * ascending, ties broken by lower index.                                   */
 int affb_knn(const void* query, const void* ref, int dtype, int64_t B, int64_t M,
              int64_t N, int D, int K, int64_t* out_idx, void* stream);
+/* 2-D K-nearest neighbours through a uniform grid of the reference points:
+ * same contract and result as affb_knn with D = 2, for fp32 points.
+ * workspace: affb_knn2d_workspace_bytes(B, N) bytes, 256-byte aligned.    */
+int64_t affb_knn2d_workspace_bytes(int64_t B, int64_t N);
+int affb_knn2d(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int K,
+               int64_t* out_idx, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* -------------------------------------------------- weighted features --
  * Replaces WeightedFeaturesFunction (src/layers/kernels/weighted_features.py:401)

@@ -600,3 +600,30 @@ def test_fused_residual_dropout_layer_norm(cuda, p):
     rx, rd = torch.autograd.grad(ref, (xr, dr), gy)
     assert rel_err(dx.cpu(), rx.cpu()) < 1e-4
     assert rel_err(dd.float().cpu(), rd.cpu()) < 8e-3
+
+
+@pytest.mark.gpu
+def test_knn2d_grid_far_queries_and_duplicates(cuda):
+    """Grid search: duplicated reference points (ties broken by index), queries
+    far outside the points' bounding box and exactly on cell edges; equal to
+    the oracle and to the brute-force entry point."""
+    from affmae_b200 import _native as nat
+    from affmae_b200.kernels.knn import knn
+    gen = torch.Generator().manual_seed(17)
+    r = torch.randint(0, 40, (2, 1500, 2), generator=gen).float()
+    r[:, 700:900] = r[:, :200]                                   # exact duplicates
+    q = torch.cat([torch.rand((2, 100, 2), generator=gen) * 40,
+                   torch.tensor([[-500.0, 3.0], [1e4, 1e4], [20.0, -300.0], [39.0, 39.0]]).expand(2, 4, 2),
+                   r[:, :50] + 0.5], dim=1)
+    import affmae_b200.kernels.knn as kmod
+    old = kmod.GRID_MIN_PAIRS
+    kmod.GRID_MIN_PAIRS = 0  # force the grid path at this size
+    for K in (1, 7, 48, 130):
+        idx = knn(q.to(cuda), r.to(cuda), K)
+        assert torch.equal(idx.cpu(), oracle.knn(q, r, K)), K
+        brute = torch.empty_like(idx)
+        qc, rc = q.to(cuda).contiguous(), r.to(cuda).contiguous()
+        nat.call("affb_knn", nat.ptr(qc), nat.ptr(rc), nat.F32, 2, q.shape[1], r.shape[1], 2, K, nat.ptr(brute),
+                 nat.stream(qc.device))
+        assert torch.equal(idx, brute), K
+    kmod.GRID_MIN_PAIRS = old

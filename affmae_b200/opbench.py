@@ -1,0 +1,127 @@
+"""Per-operator timings at the benchmark configurations' shapes.
+
+``python -m affmae_b200.opbench <op> [--iters N]`` times one operator on the
+GPU with CUDA events (inputs resident, L2 flushed by a 256 MiB write before
+every call) and prints one JSON line with its algorithmic bytes and achieved
+GB/s; the same command under ``ncu -k <kernel>`` gives the kernel profiles.
+
+  knn        config 2: B=8, N=9216 jittered lattice, queries = points, K=48
+  knn-brute  the same through the brute-force scan
+  deform     config 4, one level (96x96 kv lattice): B=16, Nq=9216, H=8, C=32, bf16, fwd+bwd
+  wfeat      config 5 stage-1 merging: weights [16,13107,48,4], feat [16,32768,96] bf16, fwd+bwd
+  wgather    config 1: idx [2,1024,48], softmax weights, feat [2,4096,128] fp32, fwd+bwd
+
+Algorithmic bytes count every interface tensor once (inputs read, outputs
+written), as the roofline of a gather-bound operator.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def _time(fn, iters, flush):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        flush.fill_(1)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(b)
+    return total / iters
+
+
+def _nbytes(*ts):
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
+def op_knn(brute=False):
+    from .kernels import knn as kmod
+    from .workloads import knn_points
+    if brute:
+        kmod.GRID_MIN_POINTS = 1 << 40
+    pos = knn_points(B=8, side=96, stride=4, device="cuda")
+    K = 48
+    out = kmod.knn(pos, pos, K)
+    B, N, _ = pos.shape
+    return (lambda: kmod.knn(pos, pos, K)), B * (N * 8 + N * 8 + N * K * 8), {
+        "B": B, "N": N, "M": N, "K": K, "path": "brute" if brute else "grid", "out": list(out.shape)}
+
+
+def op_deform():
+    from .kernels.fused_deform_attn import FusedKNNDeformCrossAttnFunction
+    from .workloads import deform_inputs
+    d = deform_inputs(B=16, side=96, level_side=96, H=8, C=32, dtype=torch.bfloat16, device="cuda")
+    leaves = {k: d[k].detach().clone().requires_grad_(k in ("offsets", "attn_weights", "values"))
+              for k in ("query_pos", "kv_pos", "offsets", "attn_weights", "values")}
+
+    def step():
+        out = FusedKNNDeformCrossAttnFunction.apply(leaves["query_pos"], leaves["kv_pos"], leaves["offsets"],
+                                                    leaves["attn_weights"], leaves["values"], d["power"], 2)
+        out.backward(d["dout"])
+    fwd = _nbytes(leaves["values"], leaves["offsets"], leaves["attn_weights"], leaves["query_pos"], leaves["kv_pos"],
+                  d["dout"])
+    bwd = fwd + _nbytes(d["dout"], leaves["values"], leaves["offsets"], leaves["attn_weights"], leaves["query_pos"])
+    return step, fwd + bwd, {"B": 16, "Nq": 9216, "Nkv": 9216, "H": 8, "C": 32, "dtype": "bf16",
+                             "pass": "fwd+bwd"}
+
+
+def op_wfeat():
+    from .kernels.weighted_features import weighted_features
+    g = torch.Generator().manual_seed(0)
+    B, No, M, IC, N, C = 16, 13107, 48, 4, 32768, 96
+    w = torch.randn((B, No, M, IC), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
+    f = torch.randn((B, N, C), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
+    idx = torch.randint(0, N, (B, No, M), generator=g).to("cuda")
+    dout = torch.randn((B, No, IC, C), generator=g).to("cuda", torch.bfloat16)
+
+    def step():
+        weighted_features(w, f, idx).backward(dout)
+    fwd = _nbytes(w, f, idx, dout)
+    bwd = _nbytes(dout, w, f, idx) + _nbytes(w, f)
+    return step, fwd + bwd, {"B": B, "No": No, "M": M, "IC": IC, "N": N, "C": C, "dtype": "bf16",
+                             "pass": "fwd+bwd"}
+
+
+def op_wgather():
+    from .kernels.weighted_gather import weighted_gather
+    g = torch.Generator().manual_seed(0)
+    B, Mq, K, N, C = 2, 1024, 48, 4096, 128
+    idx = torch.randint(0, N, (B, Mq, K), generator=g).to("cuda")
+    w = torch.softmax(torch.randn((B, Mq, K), generator=g), -1).to("cuda").requires_grad_(True)
+    f = torch.randn((B, N, C), generator=g).to("cuda").requires_grad_(True)
+    dout = torch.randn((B, Mq, C), generator=g).to("cuda")
+
+    def step():
+        weighted_gather(idx, w, f).backward(dout)
+    fwd = _nbytes(idx, w, f, dout)
+    bwd = _nbytes(dout, idx, w, f) + _nbytes(w, f)
+    return step, fwd + bwd, {"B": B, "M": Mq, "K": K, "N": N, "C": C, "dtype": "fp32", "pass": "fwd+bwd"}
+
+
+OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_deform, "wfeat": op_wfeat,
+       "wgather": op_wgather}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=sorted(OPS))
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    fn, nbytes, cfg = OPS[a.op]()
+    ms = _time(fn, a.iters, flush)
+    print(json.dumps({"op": a.op, "ms": ms, "algorithmic_bytes": nbytes, "GB_per_s": nbytes / ms / 1e6,
+                      "config": cfg}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

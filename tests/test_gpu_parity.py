@@ -33,9 +33,22 @@ def test_knn_golden(cuda, tag):
     assert torch.equal(idx.cpu(), g["idx"])
 
 
+@pytest.fixture(params=["brute", "grid"])
+def knn_path(request):
+    """Runs a KNN test through the brute-force scan and through the 2-D grid search."""
+    import affmae_b200.kernels.knn as kmod
+    old = kmod.GRID_MIN_POINTS, kmod.GRID_MIN_PAIRS
+    if request.param == "grid":
+        kmod.GRID_MIN_POINTS, kmod.GRID_MIN_PAIRS = 1, 0
+    else:
+        kmod.GRID_MIN_POINTS = 1 << 40
+    yield request.param
+    kmod.GRID_MIN_POINTS, kmod.GRID_MIN_PAIRS = old
+
+
 @pytest.mark.parametrize("K", [1, 6, 16, 33, 48, 100, 256])
 @pytest.mark.parametrize("D", [2, 3, 4])
-def test_knn_random_exact(cuda, K, D):
+def test_knn_random_exact(cuda, K, D, knn_path):
     from affmae_b200.kernels.knn import knn
     gen = torch.Generator().manual_seed(K * 10 + D)
     q = torch.rand((2, 301, D), generator=gen) * 50
@@ -45,7 +58,7 @@ def test_knn_random_exact(cuda, K, D):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_knn_ties_and_low_precision(cuda, dtype):
+def test_knn_ties_and_low_precision(cuda, dtype, knn_path):
     from affmae_b200.kernels.knn import knn
     gen = torch.Generator().manual_seed(7)
     q = torch.randint(0, 20, (3, 200, 2), generator=gen).to(dtype)

@@ -15,6 +15,8 @@
 // neighbour indices and weights are loaded once per 32 neighbours, one per
 // lane, and broadcast with shuffles.  The op is gather-bound: the feature
 // rows are the only large traffic, read once per (row, neighbour).
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace affb {
@@ -348,9 +350,18 @@ static void launch_wf(bool bwd, const T* dout, const T* w, const T* feat, const 
 }
 
 template <typename T>
+bool wf_fwd_tc(const T* w, const T* feat, const int32_t* idx, int64_t B, int64_t No, int M, int IC, int64_t N,
+               int C, T* out, cudaStream_t st, int* err);
+
+template <typename T>
 static void run_wf(bool bwd, const T* dout, const T* w, const T* feat, const int32_t* idx,
                    int64_t B, int64_t No, int M, int IC, int64_t N, int C, T* out, T* dw,
                    float* dfeat, cudaStream_t st) {
+  if constexpr (!std::is_same<T, float>::value) {
+    // 16-bit features: the forward runs on the tensor cores (wf_tc.cu)
+    int err = AFFB_OK;
+    if (!bwd && wf_fwd_tc<T>(w, feat, idx, B, No, M, IC, N, C, out, st, &err)) return;
+  }
   const bool vec = (C % 8 == 0) && ((uintptr_t)feat % 16 == 0) &&
                    (bwd ? ((uintptr_t)dout % 16 == 0 && (uintptr_t)dfeat % 16 == 0)
                         : ((uintptr_t)out % 16 == 0));

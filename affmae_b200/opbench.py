@@ -9,6 +9,7 @@ GB/s; the same command under ``ncu -k <kernel>`` gives the kernel profiles.
   knn-brute  the same through the brute-force scan
   deform     config 4, one level (96x96 kv lattice): B=16, Nq=9216, H=8, C=32, bf16, fwd+bwd
   wfeat      config 5 stage-1 merging: weights [16,13107,48,4], feat [16,32768,96] bf16, fwd+bwd
+  wfeat-fwd  the same, forward only
   wgather    config 1: idx [2,1024,48], softmax weights, feat [2,4096,128] fp32, fwd+bwd
 
 Algorithmic bytes count every interface tensor once (inputs read, outputs
@@ -74,7 +75,7 @@ def op_deform():
                              "pass": "fwd+bwd"}
 
 
-def op_wfeat():
+def op_wfeat(fwd_only=False):
     from .kernels.weighted_features import weighted_features
     g = torch.Generator().manual_seed(0)
     B, No, M, IC, N, C = 16, 13107, 48, 4, 32768, 96
@@ -82,6 +83,13 @@ def op_wfeat():
     f = torch.randn((B, N, C), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
     idx = torch.randint(0, N, (B, No, M), generator=g).to("cuda")
     dout = torch.randn((B, No, IC, C), generator=g).to("cuda", torch.bfloat16)
+
+    if fwd_only:
+        def step():
+            with torch.no_grad():
+                weighted_features(w, f, idx)
+        return step, _nbytes(w, f, idx, dout), {"B": B, "No": No, "M": M, "IC": IC, "N": N, "C": C,
+                                                "dtype": "bf16", "pass": "fwd"}
 
     def step():
         weighted_features(w, f, idx).backward(dout)
@@ -108,6 +116,7 @@ def op_wgather():
 
 
 OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_deform, "wfeat": op_wfeat,
+       "wfeat-fwd": lambda: op_wfeat(fwd_only=True),
        "wgather": op_wgather}
 
 

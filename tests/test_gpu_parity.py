@@ -203,9 +203,10 @@ def test_weighted_gather_golden(cuda):
     assert rel_err(f.grad.cpu(), g["dfeat"]) < TOL_BWD
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_LP)])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_LP), (torch.float16, TOL_LP)])
 @pytest.mark.parametrize("shape", [(2, 300, 48, 4, 700, 96), (2, 100, 48, 1, 4096, 128), (1, 50, 7, 3, 60, 13),
-                                   (1, 20, 40, 9, 30, 24)])
+                                   (1, 20, 40, 9, 30, 24), (1, 33, 17, 8, 50, 16), (1, 40, 5, 2, 64, 80),
+                                   (1, 10, 48, 4, 100, 384), (1, 7, 1, 3, 9, 32)])
 def test_weighted_features_random(cuda, dtype, tol, shape):
     from affmae_b200.kernels.weighted_features import weighted_features_fwd, weighted_features_bwd
     B, No, M, IC, N, C = shape

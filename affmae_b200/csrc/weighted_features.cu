@@ -354,13 +354,18 @@ bool wf_fwd_tc(const T* w, const T* feat, const int32_t* idx, int64_t B, int64_t
                int C, T* out, cudaStream_t st, int* err);
 
 template <typename T>
+bool wf_bwd_tc(const T* dout, const T* w, const T* feat, const int32_t* idx, int64_t B, int64_t No, int M, int IC,
+               int64_t N, int C, T* dw, float* dfeat, cudaStream_t st, int* err);
+
+template <typename T>
 static void run_wf(bool bwd, const T* dout, const T* w, const T* feat, const int32_t* idx,
                    int64_t B, int64_t No, int M, int IC, int64_t N, int C, T* out, T* dw,
                    float* dfeat, cudaStream_t st) {
   if constexpr (!std::is_same<T, float>::value) {
-    // 16-bit features: the forward runs on the tensor cores (wf_tc.cu)
+    // 16-bit features run on the tensor cores (wf_tc.cu)
     int err = AFFB_OK;
     if (!bwd && wf_fwd_tc<T>(w, feat, idx, B, No, M, IC, N, C, out, st, &err)) return;
+    if (bwd && wf_bwd_tc<T>(dout, w, feat, idx, B, No, M, IC, N, C, dw, dfeat, st, &err)) return;
   }
   const bool vec = (C % 8 == 0) && ((uintptr_t)feat % 16 == 0) &&
                    (bwd ? ((uintptr_t)dout % 16 == 0 && (uintptr_t)dfeat % 16 == 0)

@@ -261,7 +261,9 @@ class Stage(nn.Module):
 class PatchEmbed(nn.Module):
     """Stride-2 3x3 convolutions down to patch resolution; the token mask is
     re-applied after every convolution so masked patches never leak into
-    visible tokens (reference aff.py:558-665)."""
+    visible tokens (reference aff.py:558-665).  The convolutions run channels
+    last, so the channel LayerNorms see contiguous [.., C] rows and run on the
+    fused kernel without a transpose copy."""
 
     def __init__(self, patch_size: int, in_chans: int, dim: int):
         super().__init__()
@@ -275,20 +277,22 @@ class PatchEmbed(nn.Module):
             out = dim if i == layers - 1 else dim // 2
             self.convs.append(nn.Conv2d(ch, out, 3, stride=2, padding=1))
             if i < layers - 1:
-                self.norms.append(nn.LayerNorm(out))
+                self.norms.append(FusedLayerNorm(out))
             ch = out
-        self.norm = nn.LayerNorm(dim)
+        self.norm = FusedLayerNorm(dim)
 
     def forward(self, x, token_mask):
         """x [B,C,H,W]; token_mask [B, H/p, W/p] (1 visible, 0 masked)."""
+        x = x.contiguous(memory_format=torch.channels_last)
         for i, conv in enumerate(self.convs):
             x = conv(x)
             scale = max(self.patch_size >> (i + 1), 1)
             x = x * token_mask.to(x.dtype).repeat_interleave(scale, 1).repeat_interleave(scale, 2)[:, None]
             if i < len(self.norms):
-                x = F.gelu(self.norms[i](x.permute(0, 2, 3, 1)).permute(0, 3, 1, 2))
+                y = self.norms[i](x.permute(0, 2, 3, 1), out32=False, out16=True)
+                x = F.gelu(y).permute(0, 3, 1, 2)
         B, C, h, w = x.shape
-        feat = self.norm(x.flatten(2).transpose(1, 2))
+        feat = self.norm(x.permute(0, 2, 3, 1).reshape(B, h * w, C))
         ys, xs = torch.meshgrid(torch.arange(h, device=x.device), torch.arange(w, device=x.device), indexing="ij")
         pos = torch.stack([xs, ys], -1).reshape(1, -1, 2).expand(B, -1, -1).float()
         return pos, feat, h, w

@@ -8,6 +8,9 @@ GB/s; the same command under ``ncu -k <kernel>`` gives the kernel profiles.
   knn        config 2: B=8, N=9216 jittered lattice, queries = points, K=48
   knn-brute  the same through the brute-force scan
   deform     config 4, one level (96x96 kv lattice): B=16, Nq=9216, H=8, C=32, bf16, fwd+bwd
+  deform-mae config 5 decoder self-attention: B=16, 32768 masked-patch queries of a 256x256
+             lattice in random order, kv = the queries, H=6, C=64, bf16, fwd+bwd
+  deform-mae-raster  the same with the queries in raster order
   wfeat      config 5 stage-1 merging: weights [16,13107,48,4], feat [16,32768,96] bf16, fwd+bwd
   wfeat-fwd  the same, forward only
   wgather    config 1: idx [2,1024,48], softmax weights, feat [2,4096,128] fp32, fwd+bwd
@@ -75,6 +78,42 @@ def op_deform():
                              "pass": "fwd+bwd"}
 
 
+def op_deform_mae(raster=False):
+    from .kernels.fused_deform_attn import FusedKNNDeformCrossAttnFunction
+    import math
+    g = torch.Generator().manual_seed(0)
+    B, side, H, C = 16, 256, 6, 64
+    L = side * side
+    Nq = L // 2
+    ids = torch.rand((B, L), generator=g).argsort(1)[:, L - Nq:]
+    if raster:
+        ids = ids.sort(1).values
+    ii = torch.arange(side).float()
+    ys, xs = torch.meshgrid(ii, ii, indexing="ij")
+    lat = torch.stack([xs, ys], -1).reshape(-1, 2)
+    pos = lat[ids]  # masked patch positions in random order, as the decoder queries
+    theta = torch.arange(H).float() * (2 * math.pi / H)
+    d = torch.stack([theta.cos(), theta.sin()], -1)
+    d = (d / d.abs().max(-1, keepdim=True)[0])[:, None] * torch.arange(1, 5).float()[None, :, None]
+    off = d[None, None] + 0.5 * torch.randn((B, Nq, H, 4, 2), generator=g)
+    aw = torch.softmax(torch.randn((B, Nq, H, 4), generator=g), -1)
+    val = torch.randn((B, Nq, H, C), generator=g)
+    dout = torch.randn((B, Nq, H, C), generator=g).to("cuda", torch.bfloat16)
+    qp = pos.to("cuda")
+    leaves = {"offsets": off.to("cuda").requires_grad_(True), "attn_weights": aw.to("cuda").requires_grad_(True),
+              "values": val.to("cuda", torch.bfloat16).requires_grad_(True)}
+    power = torch.tensor(1.0, device="cuda")
+
+    def step():
+        out = FusedKNNDeformCrossAttnFunction.apply(qp, qp, leaves["offsets"], leaves["attn_weights"],
+                                                    leaves["values"], power, 2)
+        out.backward(dout)
+    fwd = _nbytes(leaves["values"], leaves["offsets"], leaves["attn_weights"], qp, qp, dout)
+    bwd = fwd + _nbytes(dout, leaves["values"], leaves["offsets"], leaves["attn_weights"], qp)
+    return step, fwd + bwd, {"B": B, "Nq": Nq, "Nkv": Nq, "H": H, "C": C, "dtype": "bf16", "pass": "fwd+bwd",
+                             "queries": "masked patches of a 256x256 lattice, " + ("raster order" if raster else "random order")}
+
+
 def op_wfeat(fwd_only=False):
     from .kernels.weighted_features import weighted_features
     g = torch.Generator().manual_seed(0)
@@ -115,7 +154,8 @@ def op_wgather():
     return step, fwd + bwd, {"B": B, "M": Mq, "K": K, "N": N, "C": C, "dtype": "fp32", "pass": "fwd+bwd"}
 
 
-OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_deform, "wfeat": op_wfeat,
+OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_deform, "deform-mae": op_deform_mae,
+       "deform-mae-raster": lambda: op_deform_mae(raster=True), "wfeat": op_wfeat,
        "wfeat-fwd": lambda: op_wfeat(fwd_only=True),
        "wgather": op_wgather}
 

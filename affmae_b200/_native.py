@@ -44,6 +44,7 @@ SIGNATURES = {
     "affb_layer_norm_bwd": [_p, _p, _p, _i32, _p, _p, _p, _f32, _u32, _i64, _i64, _p, _p, _i32, _p, _p,
                             _p],
     "affb_rel_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p],
+    "affb_head_copy": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "affb_pos_bias_bwd": [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "affb_deform_knn_fwd": [_p, _p, _p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _p, _p,
                             _p, _p, _p],

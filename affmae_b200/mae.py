@@ -37,6 +37,7 @@ import torch.nn.functional as F
 
 from .kernels.fused_deform_attn import (fused_knn_deformable_cross_attention,
                                         fused_knn_deformable_self_attention)
+from .kernels.head_layout import merge_heads, split_heads
 from .kernels.knn import knn
 from .kernels.layer_norm import FusedLayerNorm
 from .kernels.local_attn import FlashLocalAttentionFunction
@@ -168,14 +169,13 @@ class ClusterAttention(nn.Module):
     def forward(self, feat, member_idx, mask, pe_idx):
         B, N, C = feat.shape
         H, d = self.heads, C // self.heads
-        q = self.q(feat).view(B, N, H, d).permute(0, 2, 1, 3).contiguous()
-        kv = self.kv(feat).view(B, N, H, 2 * d).permute(0, 2, 1, 3)
-        k, v = kv[..., :d].contiguous(), kv[..., d:].contiguous()
+        q = split_heads(self.q(feat), H)
+        k, v = split_heads(self.kv(feat), H, 2)
         bias = rel_pos_bias(self.pos_embed.weight, self.pos_embed.bias, pe_idx, q.dtype)  # [B,H,N,M]
         out = FlashLocalAttentionFunction.apply(
             q, k, v, member_idx, bias, None if mask is None else mask[:, None],
             self.blank_k.view(H, d), self.blank_v.view(H, d), float(self.scale))
-        return self.proj(out.permute(0, 2, 1, 3).reshape(B, N, C))
+        return self.proj(merge_heads(out))
 
 
 class ClusterBlock(nn.Module):

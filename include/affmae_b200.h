@@ -126,6 +126,18 @@ int affb_rel_bias_fwd(const float* weight, const float* bias, const int64_t* pe_
 int affb_rel_bias_bwd(const void* dbias, const int64_t* pe_idx, int dtype, int64_t H, int64_t B,
                       int64_t N, int64_t M, float* dweight, float* dbias_vec, void* stream);
 
+/* ------------------------------------------------------- head layout --
+ * The per-head splits and merges of ClusterAttention
+ * (src/layers/attention.py:126-207: q / kv projections viewed as
+ * [B,N,H,d] and permuted to [B,H,N,d], the output permuted back), and their
+ * gradients: dst[b,n,h,j] = src[b,n,h,j] for j < d, each side addressed by
+ * its own batch / token / head strides in elements, d contiguous.
+ * elem_bytes 2 or 4; d * elem_bytes, every stride * elem_bytes and both
+ * pointers multiples of 16 bytes.                                          */
+int affb_head_copy(const void* src, int64_t src_sb, int64_t src_sn, int64_t src_sh, void* dst,
+                   int64_t dst_sb, int64_t dst_sn, int64_t dst_sh, int64_t elem_bytes, int64_t B,
+                   int64_t N, int64_t H, int64_t d, void* stream);
+
 /* ------------------------------- fused residual + dropout + LayerNorm --
  * The add / dropout / LayerNorm / dtype-cast sequences around the operators
  * above in the model (decoder blocks, src/layers/decoder.py:114-143, and the

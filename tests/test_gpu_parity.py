@@ -641,3 +641,28 @@ def test_knn2d_grid_far_queries_and_duplicates(cuda):
                  nat.stream(qc.device))
         assert torch.equal(idx, brute), K
     kmod.GRID_MIN_PAIRS = old
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("parts", [1, 2])
+def test_head_split_merge(cuda, dtype, parts):
+    """Head splits / merges of ClusterAttention are exact permute copies, and
+    so are their gradients."""
+    from affmae_b200.kernels.head_layout import merge_heads, split_heads
+    B, N, H, d = 2, 37, 3, 32
+    gen = torch.Generator().manual_seed(parts)
+    x = torch.randn((B, N, H * parts * d), generator=gen).to(cuda, dtype).requires_grad_(True)
+    outs = split_heads(x, H, parts)
+    outs = (outs,) if parts == 1 else outs
+    ref = x.detach().view(B, N, H, parts, d).permute(3, 0, 2, 1, 4)
+    for p in range(parts):
+        assert outs[p].is_contiguous() and torch.equal(outs[p], ref[p])
+    gs = [torch.randn((B, H, N, d), generator=gen).to(cuda, dtype) for _ in range(parts)]
+    torch.autograd.backward(list(outs), gs)
+    assert torch.equal(x.grad, torch.stack(gs, 0).permute(1, 3, 2, 0, 4).reshape(B, N, H * parts * d))
+    o = torch.randn((B, H, N, d), generator=gen).to(cuda, dtype).requires_grad_(True)
+    y = merge_heads(o)
+    assert torch.equal(y, o.detach().permute(0, 2, 1, 3).reshape(B, N, H * d))
+    gy = torch.randn(y.shape, generator=gen).to(cuda, dtype)
+    y.backward(gy)
+    assert torch.equal(o.grad, gy.view(B, N, H, d).permute(0, 2, 1, 3))

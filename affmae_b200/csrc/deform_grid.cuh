@@ -73,18 +73,21 @@ struct Top4 {
   __device__ __forceinline__ static bool before(float da, int ia, float db, int ib) {
     return da < db || (da == db && ia < ib);
   }
+  // Sorted insertion of (dd, ii) when it ranks before the 4th entry: one
+  // guard compare, then selects only (no nested branches, so lanes of a warp
+  // that insert at different depths do not serialise).
   __device__ __forceinline__ void offer(float dd, int ii) {
     if (!before(dd, ii, d[3], i[3])) return;
-    if (before(dd, ii, d[2], i[2])) {
-      d[3] = d[2]; i[3] = i[2];
-      if (before(dd, ii, d[1], i[1])) {
-        d[2] = d[1]; i[2] = i[1];
-        if (before(dd, ii, d[0], i[0])) {
-          d[1] = d[0]; i[1] = i[0];
-          d[0] = dd; i[0] = ii;
-        } else { d[1] = dd; i[1] = ii; }
-      } else { d[2] = dd; i[2] = ii; }
-    } else { d[3] = dd; i[3] = ii; }
+    const bool b0 = before(dd, ii, d[0], i[0]), b1 = before(dd, ii, d[1], i[1]),
+               b2 = before(dd, ii, d[2], i[2]);
+    d[3] = b2 ? d[2] : dd;
+    i[3] = b2 ? i[2] : ii;
+    d[2] = b1 ? d[1] : (b2 ? dd : d[2]);
+    i[2] = b1 ? i[1] : (b2 ? ii : i[2]);
+    d[1] = b0 ? d[0] : (b1 ? dd : d[1]);
+    i[1] = b0 ? i[0] : (b1 ? ii : i[1]);
+    d[0] = b0 ? dd : d[0];
+    i[0] = b0 ? ii : i[0];
   }
 };
 
@@ -118,6 +121,13 @@ __device__ __forceinline__ float grid_slack(const float* P, int G, float sx, flo
 }
 
 // Exact 4-NN of (sx, sy) among the points of batch element b.
+//
+// Square rings of cells around the sample's cell are visited until the
+// distance to the unvisited region exceeds the current 4th-best distance.
+// Rings 0 and 1 (the 3 x 3 block) are scanned first as three row runs: cells
+// are stored row-major, so the points of three adjacent cells of a row are one
+// contiguous range.  The result does not depend on the visiting order
+// (candidates are ranked by (d2, index)).
 __device__ inline void grid_knn4(const GridView& g, int64_t b, float sx, float sy, Top4& top) {
   top.init();
   const float* P = g.params + b * 8;
@@ -131,20 +141,28 @@ __device__ inline void grid_knn4(const GridView& g, int64_t b, float sx, float s
   // slack for the rounding of cell assignment and of boundary positions
   const float slack = 1e-4f * fmaxf(cw, ch) +
                       2e-6f * (fabsf(sx) + fabsf(sy) + fabsf(minx) + fabsf(miny) + G * fmaxf(cw, ch));
-  for (int r = 0; r <= G; ++r) {
+  auto scan_run = [&](int c0, int c1) {  // cells c0 .. c1 of one row
+    const int e = st[c1 + 1];
+    for (int t = st[c0]; t < e; ++t) {
+      const float4 q = pts[t];
+      top.offer(sqdist2(sx, sy, q.x, q.y), __float_as_int(q.z));
+    }
+  };
+  {
+    const int xlo = max(cx - 1, 0), xhi = min(cx + 1, G - 1);
+    for (int yy = max(cy - 1, 0); yy <= min(cy + 1, G - 1); ++yy) scan_run(yy * G + xlo, yy * G + xhi);
+  }
+  for (int r = 1; r <= G; ++r) {
     const int x0 = cx - r, x1 = cx + r, y0 = cy - r, y1 = cy + r;
-    const int ylo = max(y0, 0), yhi = min(y1, G - 1);
-    const int xlo = max(x0, 0), xhi = min(x1, G - 1);
-    for (int yy = ylo; yy <= yhi; ++yy) {
-      const bool edge_row = (yy == y0 || yy == y1);
-      const int step = edge_row ? 1 : (x1 - x0 > 0 ? x1 - x0 : 1);
-      for (int xx = edge_row ? xlo : x0; xx <= xhi; xx += step) {
-        if (xx < 0) continue;
-        const int c = yy * G + xx;
-        const int e = st[c + 1];
-        for (int t = st[c]; t < e; ++t) {
-          const float4 q = pts[t];
-          top.offer(sqdist2(sx, sy, q.x, q.y), __float_as_int(q.z));
+    if (r >= 2) {
+      const int ylo = max(y0, 0), yhi = min(y1, G - 1);
+      const int xlo = max(x0, 0), xhi = min(x1, G - 1);
+      for (int yy = ylo; yy <= yhi; ++yy) {
+        if (yy == y0 || yy == y1) {
+          scan_run(yy * G + xlo, yy * G + xhi);  // full edge row of the ring
+        } else {
+          if (x0 >= 0) scan_run(yy * G + x0, yy * G + x0);
+          if (x1 < G) scan_run(yy * G + x1, yy * G + x1);
         }
       }
     }

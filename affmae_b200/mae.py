@@ -492,10 +492,15 @@ class AFFMaskedAutoEncoder(nn.Module):
         return torch.einsum("nchpwq->nhwpqc", x).reshape(B, (H // p) * (W // p), p * p * c)
 
     def random_masking(self, B: int, L: int, device, generator=None):
+        """Uniform random split into kept and masked patch ids.  The masked ids
+        (the decoder's queries) are returned in raster order: a query's
+        prediction is compared with the target gathered by the same id, so
+        their order is free, and spatially ordered queries let the decoder's
+        deformable kernels hit cache for neighbouring queries' samples."""
         keep = int(L * (1 - self.cfg.mask_ratio))
         noise = torch.rand((B, L), device=device, generator=generator)
         ids = noise.argsort(dim=1)
-        return ids[:, :keep], ids[:, keep:]
+        return ids[:, :keep], ids[:, keep:].sort(dim=1).values
 
     def forward(self, imgs, generator=None):
         cfg = self.cfg

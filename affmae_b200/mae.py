@@ -138,6 +138,43 @@ def neighbourhood(pos: torch.Tensor, means: torch.Tensor, cmask, nbhd: int, m: i
 
 # ----------------------------------------------------------------- blocks --
 
+class _LinearFunction(torch.autograd.Function):
+    """y = x W^T + b in the autocast dtype; the backward computes the bias
+    gradient as a matrix-vector product with a ones vector (a single cuBLAS
+    GEMV over the gradient rows, fp32 accumulation) instead of a reduction
+    kernel, and dW / dX with one GEMM each."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.bfloat16)
+    def forward(ctx, x, weight, bias):
+        ctx.save_for_backward(x, weight)
+        ctx.has_bias = bias is not None
+        return F.linear(x, weight, bias)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, g):
+        x, weight = ctx.saved_tensors
+        g2 = g.reshape(-1, g.shape[-1])
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = (g2 @ weight).view(x.shape)
+        if ctx.needs_input_grad[1]:
+            dw = g2.t() @ x.reshape(-1, x.shape[-1])
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = torch.mv(g2.t(), torch.ones(g2.shape[0], device=g.device, dtype=g.dtype))
+        return dx, dw, db
+
+
+class Linear(nn.Linear):
+    """nn.Linear whose CUDA autocast path runs through _LinearFunction."""
+
+    def forward(self, x):
+        if x.is_cuda and torch.is_autocast_enabled("cuda"):
+            return _LinearFunction.apply(x, self.weight, self.bias)
+        return F.linear(x, self.weight, self.bias)
+
+
 class DropPath(nn.Module):
     def __init__(self, p: float):
         super().__init__()
@@ -159,12 +196,12 @@ class ClusterAttention(nn.Module):
         super().__init__()
         self.heads = heads
         self.scale = (dim // heads) ** -0.5
-        self.q = nn.Linear(dim, dim)
-        self.kv = nn.Linear(dim, 2 * dim)
+        self.q = Linear(dim, dim)
+        self.kv = Linear(dim, 2 * dim)
         self.blank_k = nn.Parameter(torch.randn(dim) * 0.2)
         self.blank_v = nn.Parameter(torch.randn(dim) * 0.2)
-        self.pos_embed = nn.Linear(5, heads)
-        self.proj = nn.Linear(dim, dim)
+        self.pos_embed = Linear(5, heads)
+        self.proj = Linear(dim, dim)
 
     def forward(self, feat, member_idx, mask, pe_idx):
         B, N, C = feat.shape
@@ -185,8 +222,8 @@ class ClusterBlock(nn.Module):
         self.attn = ClusterAttention(dim, heads)
         self.norm2 = FusedLayerNorm(dim)
         hidden = int(dim * mlp_ratio)
-        self.fc1 = nn.Linear(dim, hidden)
-        self.fc2 = nn.Linear(hidden, dim)
+        self.fc1 = Linear(dim, hidden)
+        self.fc2 = Linear(hidden, dim)
         self.drop_path = DropPath(drop_path)
 
     def forward(self, feat, member_idx, mask, pe_idx):
@@ -208,7 +245,7 @@ class ClusterMerging(nn.Module):
         self.ds_rate = ds_rate
         self.weight_net = nn.Sequential(nn.Linear(5, inner), nn.LayerNorm(inner), nn.GELU())
         self.norm = FusedLayerNorm(inner * dim)
-        self.linear = nn.Linear(inner * dim, out_dim)
+        self.linear = Linear(inner * dim, out_dim)
         self.register_buffer("rel_table", relative_position_table(), persistent=False)
 
     def forward(self, pos, feat, member_idx, mask, importance, pe_idx):
@@ -240,7 +277,7 @@ class Stage(nn.Module):
         self.blocks = nn.ModuleList(ClusterBlock(dim, heads, cfg.mlp_ratio, dp) for dp in drop_paths)
         self.merge = None
         if out_dim is not None:
-            self.prob_net = nn.Linear(dim, 1)
+            self.prob_net = Linear(dim, 1)
             self.merge = ClusterMerging(dim, out_dim, cfg.ds_rate)
 
     def forward(self, pos, feat, h, w):
@@ -370,10 +407,10 @@ class DeformableAttention(nn.Module):
     def __init__(self, dim: int, heads: int, points: int = 4):
         super().__init__()
         self.heads, self.points = heads, points
-        self.sampling_offsets = nn.Linear(dim, heads * points * 2)
-        self.attention_weights = nn.Linear(dim, heads * points)
-        self.value_proj = nn.Linear(dim, dim)
-        self.output_proj = nn.Linear(dim, dim)
+        self.sampling_offsets = Linear(dim, heads * points * 2)
+        self.attention_weights = Linear(dim, heads * points)
+        self.value_proj = Linear(dim, dim)
+        self.output_proj = Linear(dim, dim)
         self.shepard_power = nn.Parameter(torch.tensor(1.0))
         nn.init.zeros_(self.sampling_offsets.weight)
         theta = torch.arange(heads, dtype=torch.float32) * (2.0 * math.pi / heads)
@@ -412,8 +449,8 @@ class DecoderBlock(nn.Module):
         self.self_attn = DeformableAttention(dim, heads)
         self.cross_attn = DeformableAttention(dim, heads)
         self.norm1, self.norm2, self.norm3 = FusedLayerNorm(dim), FusedLayerNorm(dim), FusedLayerNorm(dim)
-        self.linear1 = nn.Linear(dim, ffn)
-        self.linear2 = nn.Linear(ffn, dim)
+        self.linear1 = Linear(dim, ffn)
+        self.linear2 = Linear(ffn, dim)
         self.p = dropout
         self.drop = nn.Dropout(dropout)
 
@@ -437,7 +474,7 @@ class PixelDecoder(nn.Module):
         super().__init__()
         D = cfg.decoder_dim
         self.dim = D
-        self.input_proj = nn.ModuleList(nn.Sequential(nn.Linear(c, D), FusedLayerNorm(D))
+        self.input_proj = nn.ModuleList(nn.Sequential(Linear(c, D), FusedLayerNorm(D))
                                         for c in reversed(cfg.embed_dims))
         for proj in self.input_proj:
             nn.init.xavier_uniform_(proj[0].weight)
@@ -464,7 +501,7 @@ class PredictionHead(nn.Module):
     def __init__(self, dim: int, out: int):
         super().__init__()
         self.norm = FusedLayerNorm(dim)
-        self.linear = nn.Linear(dim, out)
+        self.linear = Linear(dim, out)
 
     def forward(self, x):
         return self.linear(self.norm(x, out32=False, out16=True))

@@ -11,7 +11,9 @@ token.  One step = one forward + one backward call of the hot path.
   e2e   : the same bytes / time of the public autograd path
           (FlashLocalAttentionFunction.apply + backward) including the
           host->device copies of all inputs from pinned memory and the
-          device->host copies of the output and all gradients.
+          device->host copies of the output and all gradients, every step;
+          consecutive steps overlap (inputs of the next step travel in while
+          the current one computes and the previous one's results travel out).
 
 Multi-GPU: the op has no exchange step, so N GPUs run N independent replicas
 (weak scaling); value is summed over ranks using the max time over ranks.
@@ -283,38 +285,63 @@ def run_gpu(args, world, rank, local):
     achieved = bwd_bytes / (kbwd / 1e3) / 1e9
 
     # ---- e2e through the public autograd API with host buffers
+    # Every step copies its inputs from pinned host memory and reads its
+    # output and all gradients back.  Steps are pipelined over three streams:
+    # the inputs of step i+1 travel host->device while step i computes and
+    # step i-1's results travel device->host (PCIe is full duplex); device
+    # input buffers are double-buffered.
     def run_e2e():
-        host = {n: inp[n].detach().cpu().pin_memory() for n in ("q", "k", "v", "member_idx", "bias", "blank_k",
-                                                                 "blank_v", "dout")}
+        names = ("q", "k", "v", "member_idx", "bias", "blank_k", "blank_v", "dout")
+        host = {n: inp[n].detach().cpu().pin_memory() for n in names}
         h2d = sum(t.numel() * t.element_size() for t in host.values())
-
+        dev_in = [{n: torch.empty_like(t, device=dev) for n, t in host.items()} for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        in_free = [torch.cuda.Event() for _ in range(2)]
+        res_ready = [torch.cuda.Event() for _ in range(2)]
         outs_host = None
 
-        def e2e_step():
-            d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
-            leaves = {n: d[n].requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
+        def e2e_step(i):
+            nonlocal outs_host
+            k = i % 2
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(in_free[k])  # compute of step i-2 is done with these buffers
+                for n in names:
+                    dev_in[k][n].copy_(host[n], non_blocking=True)
+                in_ready[k].record(s_in)
+            stream.wait_event(in_ready[k])
+            d = dev_in[k]
+            leaves = {n: d[n].detach().requires_grad_() for n in ("q", "k", "v", "bias", "blank_k", "blank_v")}
             out = FlashLocalAttentionFunction.apply(leaves["q"], leaves["k"], leaves["v"], d["member_idx"],
                                                     leaves["bias"], None, leaves["blank_k"], leaves["blank_v"], scale)
             out.backward(d["dout"])
+            in_free[k].record(stream)
             res = [out.detach()] + [leaves[n].grad for n in ("q", "k", "v", "bias", "blank_k", "blank_v")]
-            nonlocal outs_host
+            res_ready[k].record(stream)
             if outs_host is None:  # pinned host buffers for the results, allocated once
                 outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-            for hbuf, r in zip(outs_host, res):
-                hbuf.copy_(r, non_blocking=True)
-            return outs_host
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(res_ready[k])
+                for hbuf, r in zip(outs_host, res):
+                    hbuf.copy_(r, non_blocking=True)
+                    r.record_stream(s_out)
 
-        for _ in range(max(1, args.warmup)):
-            outs_host = e2e_step()
+        for i in range(max(1, args.warmup)):
+            e2e_step(i)
         torch.cuda.synchronize()
         d2h = sum(t.numel() * t.element_size() for t in outs_host)
         barrier(world)
         torch.cuda.synchronize()
         a = torch.cuda.Event(enable_timing=True)
         c = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(args.steps):
-            outs_host = e2e_step()
+        a.record(s_in)
+        stream.wait_event(a)
+        s_out.wait_event(a)
+        for i in range(args.steps):
+            e2e_step(i)
+        done = torch.cuda.Event()
+        done.record(s_out)
+        stream.wait_event(done)
         c.record(stream)
         torch.cuda.synchronize()
         e2e_s = max_over_ranks(a.elapsed_time(c) / 1e3, world)

@@ -349,6 +349,10 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       }
     }
     __syncwarp();
+    // d_kv_pos is summed per distinct kv row of a head in shared memory (in
+    // s_w / s_cf, no longer read) and scattered once per row below
+    for (int t = lane; t < S * 4; t += 32) { s_w[warp][t] = 0.f; s_cf[warp][t] = 0.f; }
+    __syncwarp();
     float gqx = 0.f, gqy = 0.f;
     const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
     const float* kvb = kvpos + b * Nkv * 2;
@@ -382,8 +386,9 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
         const float ex = sx - kvb[2 * id], ey = sy - kvb[2 * id + 1];
         dsx = fmaf(ex, dd2, dsx);
         dsy = fmaf(ey, dd2, dsy);
-        red_add(dkvb + 2 * id, -2.f * ex * dd2);
-        red_add(dkvb + 2 * id + 1, -2.f * ey * dd2);
+        const int f = s_first[warp][s * 4 + j];
+        atomicAdd(&s_w[warp][f], -2.f * ex * dd2);
+        atomicAdd(&s_cf[warp][f], -2.f * ey * dd2);
       }
       dsx *= 2.f;
       dsy *= 2.f;
@@ -391,6 +396,13 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       d_off[2 * gs + 1] = dsy;
       gqx += dsx;
       gqy += dsy;
+    }
+    __syncwarp();
+    for (int t = lane; t < S * 4; t += 32) {
+      if (s_first[warp][t] != t) continue;
+      const int id = s_idx[warp][t];
+      red_add(dkvb + 2 * id, s_w[warp][t]);
+      red_add(dkvb + 2 * id + 1, s_cf[warp][t]);
     }
     gqx = warp_sum(gqx);
     gqy = warp_sum(gqy);

@@ -357,15 +357,17 @@ template <typename T>
 bool wf_bwd_tc(const T* dout, const T* w, const T* feat, const int32_t* idx, int64_t B, int64_t No, int M, int IC,
                int64_t N, int C, T* dw, float* dfeat, cudaStream_t st, int* err);
 
+// Returns AFFB_OK, or the error of a tensor-core launch that was chosen but
+// could not be configured (its message is already set; nothing was launched).
 template <typename T>
-static void run_wf(bool bwd, const T* dout, const T* w, const T* feat, const int32_t* idx,
-                   int64_t B, int64_t No, int M, int IC, int64_t N, int C, T* out, T* dw,
-                   float* dfeat, cudaStream_t st) {
+static int run_wf(bool bwd, const T* dout, const T* w, const T* feat, const int32_t* idx,
+                  int64_t B, int64_t No, int M, int IC, int64_t N, int C, T* out, T* dw,
+                  float* dfeat, cudaStream_t st) {
   if constexpr (!std::is_same<T, float>::value) {
     // 16-bit features run on the tensor cores (wf_tc.cu)
     int err = AFFB_OK;
-    if (!bwd && wf_fwd_tc<T>(w, feat, idx, B, No, M, IC, N, C, out, st, &err)) return;
-    if (bwd && wf_bwd_tc<T>(dout, w, feat, idx, B, No, M, IC, N, C, dw, dfeat, st, &err)) return;
+    if (!bwd && wf_fwd_tc<T>(w, feat, idx, B, No, M, IC, N, C, out, st, &err)) return err;
+    if (bwd && wf_bwd_tc<T>(dout, w, feat, idx, B, No, M, IC, N, C, dw, dfeat, st, &err)) return err;
   }
   const bool vec = (C % 8 == 0) && ((uintptr_t)feat % 16 == 0) &&
                    (bwd ? ((uintptr_t)dout % 16 == 0 && (uintptr_t)dfeat % 16 == 0)
@@ -376,6 +378,7 @@ static void run_wf(bool bwd, const T* dout, const T* w, const T* feat, const int
   else
     for (int ic0 = 0; ic0 < IC; ic0 += 8)
       launch_wf<T, 8>(bwd, dout, w, feat, idx, B, No, M, IC, ic0, N, C, vec, out, dw, dfeat, st);
+  return AFFB_OK;
 }
 
 static int check_wf(int64_t B, int64_t No, int64_t M, int64_t IC, int64_t N, int64_t C) {
@@ -396,9 +399,11 @@ extern "C" int affb_weighted_features_fwd(const void* w, const void* feat, const
                                           void* stream) {
   if (int e = check_wf(B, No, M, IC, N, C)) return e;
   if (B == 0 || No == 0 || C == 0) return AFFB_OK;
+  int err = AFFB_OK;
   AFFB_DISPATCH(dtype, T,
-                run_wf<T>(false, nullptr, (const T*)w, (const T*)feat, idx, B, No, (int)M,
+                err = run_wf<T>(false, nullptr, (const T*)w, (const T*)feat, idx, B, No, (int)M,
                           (int)IC, N, (int)C, (T*)out, nullptr, nullptr, as_stream(stream)));
+  if (err != AFFB_OK) return err;
   AFFB_LAUNCH_CHECK("affb_weighted_features_fwd");
   return AFFB_OK;
 }
@@ -410,10 +415,12 @@ extern "C" int affb_weighted_features_bwd(const void* dout, const void* w, const
                                           void* stream) {
   if (int e = check_wf(B, No, M, IC, N, C)) return e;
   if (B == 0 || No == 0 || M == 0) return AFFB_OK;
+  int err = AFFB_OK;
   AFFB_DISPATCH(dtype, T,
-                run_wf<T>(true, (const T*)dout, (const T*)w, (const T*)feat, idx, B, No,
+                err = run_wf<T>(true, (const T*)dout, (const T*)w, (const T*)feat, idx, B, No,
                           (int)M, (int)IC, N, (int)C, nullptr, (T*)dw, dfeat_acc,
                           as_stream(stream)));
+  if (err != AFFB_OK) return err;
   AFFB_LAUNCH_CHECK("affb_weighted_features_bwd");
   return AFFB_OK;
 }

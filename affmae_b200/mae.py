@@ -528,24 +528,27 @@ class AFFMaskedAutoEncoder(nn.Module):
         x = imgs.reshape(B, c, H // p, p, W // p, p)
         return torch.einsum("nchpwq->nhwpqc", x).reshape(B, (H // p) * (W // p), p * p * c)
 
-    def random_masking(self, B: int, L: int, device, generator=None):
+    def random_masking(self, B: int, L: int, device, generator=None, noise=None):
         """Uniform random split into kept and masked patch ids.  The masked ids
         (the decoder's queries) are returned in raster order: a query's
         prediction is compared with the target gathered by the same id, so
         their order is free, and spatially ordered queries let the decoder's
         deformable kernels hit cache for neighbouring queries' samples."""
         keep = int(L * (1 - self.cfg.mask_ratio))
-        noise = torch.rand((B, L), device=device, generator=generator)
+        if noise is None:
+            noise = torch.rand((B, L), device=device, generator=generator)
         ids = noise.argsort(dim=1)
         return ids[:, :keep], ids[:, keep:].sort(dim=1).values
 
-    def forward(self, imgs, generator=None):
+    def forward(self, imgs, generator=None, noise=None):
+        """``noise`` [B, L] (optional) replaces the random draw that picks the
+        masked patches (the patches with the largest noise are masked)."""
         cfg = self.cfg
         B, _, H, W = imgs.shape
         p = cfg.patch_size
         patches = self.patchify(imgs)
         L = patches.shape[1]
-        ids_keep, ids_masked = self.random_masking(B, L, imgs.device, generator)
+        ids_keep, ids_masked = self.random_masking(B, L, imgs.device, generator, noise)
         token_mask = torch.ones((B, L), device=imgs.device)
         token_mask.scatter_(1, ids_masked, 0.0)
         token_mask = token_mask.view(B, H // p, W // p)

@@ -12,9 +12,10 @@ not available here; these generators stand in for them).
     attention in level-0 token units.
   * ``knn_points``: config 2 — jittered 96x96 stride-4 lattice.
 
-Curve order: the reference clusters tokens along a Hilbert/Peano curve
-(src/utils/geometry.py:170-319); a Morton (Z-order) curve is used here, which
-gives the same kind of compact 8-token clusters.
+Curve order: tokens are clustered by the reference's own space-filling scan
+of grid anchors (src/utils/geometry.py:170-319, restated bit-exactly in
+``affmae_b200.mae.curve_clusters``).  ``order="morton"`` gives the Z-order
+curve used by earlier benchmark lines, kept so both can be compared.
 """
 from __future__ import annotations
 
@@ -50,9 +51,12 @@ def _morton(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     return spread(x) | (spread(y) << 1)
 
 
-def clustered_tokens(B: int, side: int, keep: float, seed: int, device) -> torch.Tensor:
+def clustered_tokens(B: int, side: int, keep: float, seed: int, device,
+                     order: str = "curve") -> torch.Tensor:
     """Positions [B, N, 2] (fp32 grid coordinates) of the kept tokens of a
-    side x side grid, in curve order.  N = round(side*side*keep)."""
+    side x side grid, in cluster order.  N = round(side*side*keep).
+    ``order``: "curve" = the reference's anchor scan (geometry.py:170-319),
+    "morton" = Z-order."""
     g = torch.Generator().manual_seed(seed)
     n_all = side * side
     n = int(round(n_all * keep))
@@ -61,10 +65,17 @@ def clustered_tokens(B: int, side: int, keep: float, seed: int, device) -> torch
     out = torch.empty((B, n, 2))
     for b in range(B):
         sel = torch.randperm(n_all, generator=g)[:n]
-        p = grid[sel]
-        order = torch.argsort(_morton(p[:, 0], p[:, 1]))
-        out[b] = p[order].float()
-    return out.to(device)
+        out[b] = grid[sel].float()
+    if order == "morton":
+        for b in range(B):
+            o = torch.argsort(_morton(out[b, :, 0].long(), out[b, :, 1].long()))
+            out[b] = out[b][o]
+        return out.to(device)
+    if order != "curve":
+        raise ValueError(f"unknown cluster order {order!r}")
+    from .mae import curve_clusters   # the model module imports this one
+    pos, _, _, _ = curve_clusters(out, 8, side, side)
+    return pos.to(device)
 
 
 def neighbourhoods(pos: torch.Tensor, cluster: int = 8, nbhd: int = 48):
@@ -90,10 +101,10 @@ def neighbourhoods(pos: torch.Tensor, cluster: int = 8, nbhd: int = 48):
 
 
 def nbhd_attention_inputs(B=32, side=96, keep=0.5, H=4, d=32, nbhd=48, dtype=torch.bfloat16,
-                          seed=0, device="cuda"):
+                          seed=0, device="cuda", order="curve"):
     """Config 3 inputs: dict(q, k, v [B,H,N,d], member_idx [B,N,M] int32, bias [B,H,N,M],
     blank_k, blank_v [H,d], dout [B,H,N,d], scale)."""
-    pos = clustered_tokens(B, side, keep, seed, device)
+    pos = clustered_tokens(B, side, keep, seed, device, order)
     member, pe_idx = neighbourhoods(pos, 8, nbhd)
     N = pos.shape[1]
     g = torch.Generator(device="cpu").manual_seed(seed + 1)
@@ -159,3 +170,48 @@ def deform_inputs(B=16, side=96, level_side=96, H=8, C=32, dtype=torch.bfloat16,
     to = lambda t, dt=torch.float32: t.to(device=device, dtype=dt)
     return dict(query_pos=to(qpos), kv_pos=to(kv), offsets=to(off), attn_weights=to(aw),
                 values=to(val, dtype), power=torch.tensor(1.0, device=device), dout=to(dout, dtype))
+
+
+def deform_levels_inputs(B=16, side=96, level_sides=(96, 48, 24), H=8, C=32, dtype=torch.bfloat16,
+                         seed=0, device="cuda"):
+    """All levels of config 4 in level-0 token units: one query set, per level l
+    a kv lattice of level_sides[l]^2 points ((i+0.5)*s_l - 0.5), offsets
+    N(0, 0.05)*side, and the level's 4-point slice of a softmax over the
+    4*len(level_sides) (level, point) pairs of each head.  Returns
+    dict(query_pos, power, dout, levels=[dict(kv_pos, offsets, attn_weights, values)])."""
+    g = torch.Generator().manual_seed(seed)
+    L = len(level_sides)
+    Nq = side * side
+    qpos = torch.rand((B, Nq, 2), generator=g) * side - 0.5
+    aw_all = torch.softmax(torch.randn((B, Nq, H, 4 * L), generator=g), -1)
+    to = lambda t, dt=torch.float32: t.to(device=device, dtype=dt)
+    levels = []
+    for li, ls in enumerate(level_sides):
+        s = side / ls
+        ii = torch.arange(ls).float()
+        ys, xs = torch.meshgrid(ii, ii, indexing="ij")
+        kv = ((torch.stack([xs, ys], -1).reshape(1, -1, 2) + 0.5) * s - 0.5).expand(B, -1, -1).contiguous()
+        off = torch.randn((B, Nq, H, 4, 2), generator=g) * 0.05 * side
+        val = torch.randn((B, kv.shape[1], H, C), generator=g)
+        levels.append(dict(kv_pos=to(kv), offsets=to(off),
+                           attn_weights=to(aw_all[..., 4 * li:4 * li + 4].contiguous()),
+                           values=to(val, dtype)))
+    dout = torch.randn((B, Nq, H, C), generator=g)
+    return dict(query_pos=to(qpos), power=torch.tensor(1.0, device=device), dout=to(dout, dtype),
+                levels=levels)
+
+
+def deform_levels_bytes(B, Nq, level_n, H, C, elem):
+    """Interface bytes of one forward and one backward over all levels (config 4):
+    values, offsets, weights, query positions, output; the backward reads
+    dout and the inputs and writes every gradient."""
+    nkv = sum(level_n)
+    L = len(level_n)
+    val = B * nkv * H * C * elem
+    off = B * Nq * H * 4 * L * 2 * elem
+    aw = B * Nq * H * 4 * L * elem
+    qp = B * Nq * 2 * 4
+    out = B * Nq * H * C * elem
+    fwd = val + off + aw + qp + out
+    bwd = out + val + off + aw + qp + val + off + aw + qp + B * nkv * 2 * 4
+    return fwd, bwd

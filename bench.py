@@ -17,6 +17,10 @@ token.  One step = one forward + one backward call of the hot path.
 
 Multi-GPU: the op has no exchange step, so N GPUs run N independent replicas
 (weak scaling); value is summed over ranks using the max time over ranks.
+Every run also times config 5 (AFF-small MAE pretraining, 16 images per GPU)
+at the same N and reports it as the nested ``mae`` object: under DDP with an
+NCCL gradient all-reduce overlapped with the backward when WORLD_SIZE > 1
+(``--no-mae`` skips it; ``--workload mae`` runs it alone as the main line).
 
 ``--impl reference`` times the reference's pure-PyTorch formula of this op
 (the gathered-softmax formula of local_attn.py:979-1006, autograd backward)
@@ -51,6 +55,8 @@ def workload_config(extra=None):
     c = {"workload": "neighbourhood attention fwd+bwd (config 3)", "global_batch": CFG["B"],
          "tokens": int(CFG["side"] ** 2 * CFG["keep"]), "heads": CFG["H"], "head_dim": CFG["d"],
          "neighbours": CFG["nbhd"], "bias": True, "blank": True, "mask": None,
+         "cluster_order": {"curve": "reference anchor scan (geometry.py:170-319)",
+                           "morton": "Z-order"}[CFG.get("order", "curve")],
          "l2": "flushed by a 256 MiB write before every timed step"}
     if extra:
         c.update(extra)
@@ -211,7 +217,7 @@ def run_gpu(args, world, rank, local):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     nat.lib()
-    inp = nbhd_attention_inputs(B=CFG["B"], dtype=torch.bfloat16, seed=rank, device=dev,
+    inp = nbhd_attention_inputs(B=CFG["B"], dtype=torch.bfloat16, seed=rank, device=dev, order=args.order,
                                 **{k: CFG[k] for k in ("side", "keep", "H", "d", "nbhd")})
     q, k, v, mi, bias = inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["bias"]
     bk, bv, do, scale = inp["blank_k"], inp["blank_v"], inp["dout"], inp["scale"]
@@ -380,12 +386,16 @@ def run_gpu(args, world, rank, local):
                              "algorithmic_bytes": bwd_bytes, "kernel_ms": kbwd},
                 "cpu_baseline": cpu, "clocks": clocks,
                 "gpu_launches": args.steps * LAUNCHES_PER_STEP}
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
-def run_mae(args, world, rank, local):
+def run_mae(args, world, rank, local, steps=None, warmup=None):
     """Config 5: AFF-small MAE pretraining steps, data parallel over `world`
-    GPUs (DDP, NCCL all-reduce overlapped with the backward pass)."""
+    GPUs (DDP, NCCL all-reduce overlapped with the backward pass).  Returns
+    the JSON line on rank 0 (None elsewhere)."""
+    steps = steps if steps is None else steps
+    warmup = warmup if warmup is None else warmup
     from affmae_b200 import _native as nat
     from affmae_b200.mae import MAEConfig
     from affmae_b200.pretrain import build, synthetic_images, train_step
@@ -397,7 +407,7 @@ def run_mae(args, world, rank, local):
     imgs = synthetic_images(per_gpu, cfg.img_size, seed=1000 + rank, device=dev)
     gen = torch.Generator(device=dev).manual_seed(rank)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         train_step(model, opt, imgs, generator=gen)
     torch.cuda.synchronize()
     barrier(world)
@@ -407,7 +417,7 @@ def run_mae(args, world, rank, local):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             loss = train_step(model, opt, imgs, generator=gen)
         e1.record(stream)
         torch.cuda.synchronize()
@@ -422,7 +432,7 @@ def run_mae(args, world, rank, local):
         e2 = torch.cuda.Event(enable_timing=True)
         e3 = torch.cuda.Event(enable_timing=True)
         e2.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             x = host.to(dev, non_blocking=True)
             loss = train_step(model, opt, x, generator=gen)
             loss_host.copy_(loss.float(), non_blocking=True)
@@ -431,9 +441,9 @@ def run_mae(args, world, rank, local):
         e2e_s = max_over_ranks(e2.elapsed_time(e3) / 1e3, world)
     clocks = clk.summary()
     if rank == 0:
-        value = world * per_gpu * args.steps / dev_s
+        value = world * per_gpu * steps / dev_s
         line = {"metric": "AFF-small MAE pretraining img/s", "value": value, "unit": "img/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps,
+                "steps": steps, "warmup": warmup, "ms_per_step": dev_s * 1e3 / steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic N(0,1) images, normalised per image; random-init weights",
                 "config": {"workload": "AFF-small MAE pretraining step (config 5)", "global_batch": per_gpu * world,
@@ -441,13 +451,14 @@ def run_mae(args, world, rank, local):
                            "mask_ratio": cfg.mask_ratio, "nbhd": cfg.nbhd_size, "parallelism": f"ddp{world}",
                            "l2": "working set far above L2 (no flush needed)"},
                 "img_per_s_per_gpu": value / world, "final_loss": float(loss),
-                "e2e": {"value": world * per_gpu * args.steps / e2e_s, "unit": "img/s",
+                "e2e": {"value": world * per_gpu * steps / e2e_s, "unit": "img/s",
                         "h2d_bytes_per_step": host.numel() * host.element_size(), "d2h_bytes_per_step": 4,
-                        "ms_per_step": e2e_s * 1e3 / args.steps},
+                        "ms_per_step": e2e_s * 1e3 / steps},
                 "roofline": None, "cpu_baseline": None,
                 "cpu_baseline_note": "not run for config 5 (a CPU pretraining step is infeasible)",
-                "clocks": clocks, "abi_calls_per_step": calls / args.steps}
-        print(json.dumps(line), flush=True)
+                "clocks": clocks, "abi_calls_per_step": calls / steps}
+        return line
+    return None
 
 
 def main():
@@ -462,8 +473,15 @@ def main():
     ap.add_argument("--workload", default="attn", choices=["attn", "mae"],
                     help="attn: config 3 neighbourhood attention (default); mae: config 5 pretraining")
     ap.add_argument("--mae-batch", type=int, default=16, help="images per GPU for --workload mae")
+    ap.add_argument("--no-mae", action="store_true",
+                    help="attn workload: skip the config 5 pretraining leg reported as the nested 'mae' object")
+    ap.add_argument("--mae-steps", type=int, default=10, help="timed config 5 steps of the nested 'mae' leg")
+    ap.add_argument("--mae-warmup", type=int, default=3, help="warm-up config 5 steps of the nested 'mae' leg")
+    ap.add_argument("--order", default="curve", choices=["curve", "morton"],
+                    help="cluster order of the config 3 tokens: the reference's anchor scan (default) or Z-order")
     args = ap.parse_args()
     CFG["B"] = args.batch
+    CFG["order"] = args.order
     world, rank, local = dist_setup()
     if args.workload == "mae":
         if args.impl == "reference":
@@ -471,11 +489,27 @@ def main():
                 print(json.dumps({"impl": "reference", "unavailable": "the reference's MAE model needs its Triton "
                                   "GPU kernels and pykeops, which are not installed on the GPU box"}), flush=True)
         else:
-            run_mae(args, world, rank, local)
+            line = run_mae(args, world, rank, local)
+            if line is not None:
+                print(json.dumps(line), flush=True)
     elif args.impl == "reference":
         run_reference(args, world, rank)
     else:
-        run_gpu(args, world, rank, local)
+        line = run_gpu(args, world, rank, local)
+        if not args.no_mae:
+            # config 5 at the same N: data parallel under DDP when WORLD_SIZE > 1
+            torch.cuda.empty_cache()
+            m = run_mae(args, world, rank, local, steps=args.mae_steps, warmup=args.mae_warmup)
+            if line is not None:
+                line["mae"] = {"metric": m["metric"], "img_per_s": m["value"],
+                               "img_per_s_per_gpu": m["img_per_s_per_gpu"], "unit": "img/s",
+                               "ms_per_step": m["ms_per_step"], "steps": m["steps"], "warmup": m["warmup"],
+                               "per_gpu_batch": m["config"]["per_gpu_batch"],
+                               "parallelism": m["config"]["parallelism"], "e2e_img_per_s": m["e2e"]["value"],
+                               "final_loss": m["final_loss"], "clocks": m["clocks"],
+                               "workload": m["config"]["workload"]}
+        if line is not None:
+            print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

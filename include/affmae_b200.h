@@ -145,7 +145,8 @@ int affb_head_copy(const void* src, int64_t src_sb, int64_t src_sn, int64_t src_
  * Forward: s = x + dropout_p(delta) (delta may be NULL), y = LN(s) written to
  * y32 (fp32) and/or y16_bf16; rows R of C <= 1536 channels; x and delta fp32
  * or bf16; s_saved [R,C] fp32 (needed with delta), mean/rstd [R] fp32.  The
- * dropout mask is a hash of (seed, element index).                          */
+ * dropout mask is Philox-4x32-10 of (seed, element index); the same seed and
+ * p regenerate it in the backward.                                         */
 int affb_layer_norm_fwd(const void* x, int x_dtype, const void* delta, int delta_dtype, float p,
                         uint32_t seed, const float* gamma, const float* beta, float eps, int64_t R,
                         int64_t C, float* s_saved, float* mean, float* rstd, float* y32,
@@ -157,6 +158,10 @@ int affb_layer_norm_bwd(const float* dy32, const void* dy16_bf16, const void* s,
                         const float* mean, const float* rstd, const float* gamma, float p,
                         uint32_t seed, int64_t R, int64_t C, void* dx, void* ddelta,
                         int delta_dtype, float* dgamma, float* dbeta, void* stream);
+/* Host-side evaluation of that dropout mask: keep[i] = 1 when element e0 + i
+ * survives dropout p under `seed` (the kernels' exact rule).  No GPU.  Part
+ * of the model glue; the reference uses torch's dropout here.              */
+int affb_dropout_keep_mask(uint32_t seed, float p, int64_t e0, int64_t n, uint8_t* keep);
 
 /* --------------------------------- fused KNN deformable attention (2-D) --
  * Replaces fused_knn_deform_cross_attn_forward_save
@@ -194,7 +199,10 @@ int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos, const float
  * stream capture.  Every call on a device shares that device's array, which
  * keeps the last call's contents (each call clears what it needs cleared);
  * calls whose GPU work can overlap (for example on unordered streams) race
- * on it and must be serialised by the caller.                              */
+ * on it and must be serialised by the caller.  The cached address belongs to
+ * the device's primary context: do not use this entry point across a
+ * cudaDeviceReset (or a release and re-creation of the primary context) in
+ * the same process.                                                        */
 int64_t affb_deform_noalloc_max_scratch_bytes(void);
 int affb_deform_knn_fwd_noalloc(const float* query_pos, const float* kv_pos,
                                 const float* offsets, const float* attn_w, const void* values,

@@ -15,6 +15,7 @@ from .ops import (  # noqa: F401
     nbhd_attn_fwd,
     nbhd_attn_bwd,
     nbhd_attn_formula,
+    nbhd_blank_grads,
     weighted_features_fwd,
     weighted_features_bwd,
     deform_knn_fwd,

@@ -37,8 +37,16 @@ def _sqdist_f32(q, r):
 
 def _topk_stable(d, k):
     """Indices of the k smallest entries of each row, ties by lower index."""
-    # argsort with kind='stable' keeps equal keys in index order
-    return np.argsort(d, axis=-1, kind="stable")[..., :k]
+    # (d, index) packed into one unique uint64 key: non-negative fp32 values
+    # order like their bit patterns, so the key order is the (d, index) order;
+    # a partition then a sort of the k smallest keys is exact and avoids a full sort.
+    n = d.shape[-1]
+    if k >= n or d.dtype != np.float32 or (d < 0).any() or np.isnan(d).any():
+        return np.argsort(d, axis=-1, kind="stable")[..., :k]
+    key = (d.view(np.uint32).astype(np.uint64) << np.uint64(32)) | np.arange(n, dtype=np.uint64)
+    part = np.partition(key, k - 1, axis=-1)[..., :k]
+    part.sort(axis=-1)
+    return (part & np.uint64(0xFFFFFFFF)).astype(np.int64)
 
 
 def knn(query, ref, k, chunk=512):
@@ -160,6 +168,19 @@ def nbhd_attn_bwd(q, k, v, mi, scale, o, lse, do, bias=None, mask=None, blank_k=
         dbk = scale * (dsb[..., None] * q).sum((0, 2))
         dbv = (pb[..., None] * do).sum((0, 2))
     return scale * dq, dk, dv, dbias, dbk, dbv
+
+
+def nbhd_blank_grads(q, scale, lse, o, do, blank_k, blank_v):
+    """(dblank_k [H,D], dblank_v [H,D]) in float64 from the per-row blank terms
+    of nbhd_attn_bwd (local_attn.py:530-550); needs no neighbour gather, so it
+    runs on whole large batches."""
+    q, o, do, lse = _t(q, F64), _t(o, F64), _t(do, F64), _t(lse, F64)
+    bk, bv = _t(blank_k, F64), _t(blank_v, F64)
+    delta = (o * do).sum(-1)
+    sb = scale * (q * bk[None, :, None, :]).sum(-1)
+    pb = torch.exp(sb - lse)
+    dsb = pb * ((do * bv[None, :, None, :]).sum(-1) - delta)
+    return scale * (dsb[..., None] * q).sum((0, 2)), (pb[..., None] * do).sum((0, 2))
 
 
 def nbhd_attn_formula(q, k, v, mi, scale, bias=None, mask=None, blank_k=None, blank_v=None):

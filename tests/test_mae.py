@@ -119,3 +119,56 @@ def test_mae_small_training_steps(cuda):
     losses = [float(train_step(model, opt, imgs)) for _ in range(4)]
     assert all(np.isfinite(losses)), losses
     assert len(set(losses)) > 1
+
+
+def _mae_ddp_worker(rank, world, port, imgs, noise, out):
+    import torch.distributed as dist
+    from affmae_b200.mae import MAEConfig
+    from affmae_b200.pretrain import build
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    cfg = MAEConfig(img_size=128, drop_path_rate=0.0, decoder_dropout=0.0)
+    model, _ = build(cfg, device=dev, ddp=True, seed=0)
+    half = imgs.shape[0] // world
+    sl = slice(rank * half, (rank + 1) * half)
+    with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        loss, _ = model(imgs[sl].to(dev), noise=noise[sl].to(dev))
+    loss.backward()
+    grads = {n: p.grad.detach().float().cpu() for n, p in model.module.named_parameters()}
+    if rank == 0:
+        torch.save(grads, out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_mae_ddp_two_gpus_matches_single_gpu(cuda, tmp_path):
+    """Config 5's data-parallel step over NCCL on two GPUs: each rank takes half
+    of the batch; the gradients DDP all-reduces equal those of one GPU on the
+    whole batch (same weights, same masks, no dropout), within bf16 tolerance."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from affmae_b200.mae import MAEConfig
+    from affmae_b200.pretrain import build, synthetic_images
+    cfg = MAEConfig(img_size=128, drop_path_rate=0.0, decoder_dropout=0.0)
+    imgs = synthetic_images(4, 128, seed=3, device="cpu")
+    L = (128 // cfg.patch_size) ** 2
+    noise = torch.rand((4, L), generator=torch.Generator().manual_seed(4))
+    out = str(tmp_path / "ddp_grads.pt")
+    port = 29700 + (os.getpid() % 1000)
+    mp.spawn(_mae_ddp_worker, args=(2, port, imgs, noise, out), nprocs=2, join=True)
+    model, _ = build(cfg, device=cuda, ddp=False, seed=0)
+    with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        loss, _ = model(imgs.to(cuda), noise=noise.to(cuda))
+    loss.backward()
+    ddp = torch.load(out)
+    num = den = 0.0
+    for n, p in model.named_parameters():
+        g = p.grad.detach().float().cpu()
+        num += float((ddp[n] - g).pow(2).sum())
+        den += float(g.pow(2).sum())
+        assert torch.isfinite(ddp[n]).all(), n
+    assert (num / den) ** 0.5 < 2e-2, (num / den) ** 0.5

@@ -53,6 +53,36 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
         assert rel_err(got[0].float(), ref[0].float()) < 1e-5
 
 
+def test_noalloc_near_capacity(cuda):
+    """A grid that just fits the fixed array (close to its whole size): the
+    layout inside the array matches the workspace entry point bit for bit."""
+    from affmae_b200 import _native as nat
+    lib = nat.lib()
+    cap = int(lib.affb_deform_noalloc_max_scratch_bytes())
+    lo, hi = 1, cap
+    while lo < hi:  # largest kv count of one image whose grid fits
+        mid = (lo + hi + 1) // 2
+        if int(lib.affb_deform_workspace_bytes(1, mid)) <= cap:
+            lo = mid
+        else:
+            hi = mid - 1
+    nkv = lo
+    assert int(lib.affb_deform_workspace_bytes(1, nkv)) > 0.95 * cap
+    g = torch.Generator().manual_seed(3)
+    side = float(nkv) ** 0.5
+    d = dict(query_pos=(torch.rand((1, 256, 2), generator=g) * side).to(cuda),
+             kv_pos=(torch.rand((1, nkv, 2), generator=g) * side).to(cuda),
+             offsets=torch.randn((1, 256, 1, 4, 2), generator=g).to(cuda),
+             attn_weights=torch.softmax(torch.randn((1, 256, 1, 4), generator=g), -1).to(cuda),
+             values=torch.randn((1, nkv, 1, 8), generator=g).to(cuda, torch.bfloat16),
+             power=torch.tensor(1.0, device=cuda))
+    for _ in range(2):
+        ref = _run(nat, d, noalloc=False)
+        got = _run(nat, d, noalloc=True)
+        assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
+        assert torch.equal(got[0], ref[0])
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda):
     from affmae_b200 import _native as nat
     cap = int(nat.lib().affb_deform_noalloc_max_scratch_bytes())

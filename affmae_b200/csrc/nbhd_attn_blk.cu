@@ -489,8 +489,8 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpBw
                             pack2<T>(ds[1][0], ds[1][1]), pack2<T>(ds[1][2], ds[1][3])};
     mma_chunk_pv<T>(qacc, da, w.KV[buf][0], 0);
     __syncwarp();
-    mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD);
-    mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD);
+    mma_chunk_scatter<T>(w.dS, BPT, w.Q, uclu, U, c * 16, a.scale, a.dk + bh * N * TD, N);
+    mma_chunk_scatter<T>(w.P, BPT, w.dO, uclu, U, c * 16, 1.f, a.dv + bh * N * TD, N);
     __syncwarp();
   }
   const T* bkp = a.blank_k ? (const T*)a.blank_k + (int64_t)h * TD : nullptr;

@@ -33,6 +33,8 @@
 #include "nbhd_tc.cuh"
 #include "nbhd_mma.cuh"
 
+#include <type_traits>
+
 namespace affb {
 
 constexpr int KV_LCAP = 256;  // list segment held in shared memory; shorter lists are sorted
@@ -182,9 +184,32 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
 // pb = exp(q . blank_k * scale - lse), dS_blank = pb (dO . blank_v - D), and
 // the blank gradients dblank_k += dS_blank q scale, dblank_v += pb dO
 // (reference local_attn.py:526-550).  One block per PRO_ROWS rows of one
-// (b, h); four lanes per row, eight dims per lane; the blank gradients are
-// summed in registers over the block's rows and reduced once.
+// (b, h); four lanes per row, eight dims per lane; every row load of the
+// block's four passes is issued before the first is used (the kernel is a
+// stream bounded by loads in flight); the blank gradients are summed in
+// registers over the block's rows and reduced once.
 constexpr int PRO_ROWS = 256;
+constexpr int PRO_PASSES = PRO_ROWS / 64;
+
+template <typename T>
+__device__ __forceinline__ void cvt8(const uint4& u, float* o) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[2 * i] = __uint_as_float(w[i] << 16);
+      o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs& k, int64_t bid) {
@@ -204,36 +229,45 @@ __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs
     ld8((const T*)a.blank_v + (int64_t)h * TD + sub * 8, bvv);
     if (t < TD) { s_dbk[t] = 0.f; s_dbv[t] = 0.f; }
   }
-#pragma unroll 1
-  for (int r0 = 0; r0 < PRO_ROWS; r0 += 64) {
-    const int n = nbase + r0 + (t >> 2);
+  uint4 ro[PRO_PASSES], rd[PRO_PASSES], rq[PRO_PASSES];
+  float ls[PRO_PASSES];
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+  for (int it = 0; it < PRO_PASSES; ++it) {
+    const int n = nbase + it * 64 + (t >> 2);
+    const int64_t row = bh * N + (n < N ? n : 0);
+    const bool valid = n < N;
+    ro[it] = valid ? __ldg(reinterpret_cast<const uint4*>((const T*)a.o + row * TD + sub * 8)) : z4;
+    rd[it] = valid ? __ldg(reinterpret_cast<const uint4*>((const T*)a.dout + row * TD + sub * 8)) : z4;
+    rq[it] = valid && blank ? __ldg(reinterpret_cast<const uint4*>((const T*)a.q + row * TD + sub * 8)) : z4;
+    ls[it] = valid && blank ? __ldg(a.lse + row) : 0.f;
+  }
+#pragma unroll
+  for (int it = 0; it < PRO_PASSES; ++it) {
+    const int n = nbase + it * 64 + (t >> 2);
     const bool valid = n < N;
     const int64_t row = bh * N + n;
-    float ov[8], dv[8], qv[8], di = 0.f, ls = 0.f;
-    if (valid) {
-      if (blank) ls = __ldg(a.lse + row);  // issued with the row loads, used after the reductions
-      ld8((const T*)a.o + row * TD + sub * 8, ov);
-      ld8((const T*)a.dout + row * TD + sub * 8, dv);
-      if (blank) ld8((const T*)a.q + row * TD + sub * 8, qv);
+    float ov[8], dv[8], di = 0.f;
+    cvt8<T>(ro[it], ov);
+    cvt8<T>(rd[it], dv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
-    }
+    for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
     di += __shfl_xor_sync(0xffffffffu, di, 1);
     di += __shfl_xor_sync(0xffffffffu, di, 2);
     if (valid && sub == 0) k.di[row] = di;
     if (blank) {
+      float qv[8];
+      cvt8<T>(rq[it], qv);
       float sb = 0.f, dpb = 0.f;
-      if (valid) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
-      }
+      for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
 #pragma unroll
       for (int o = 1; o < 4; o <<= 1) {
         sb += __shfl_xor_sync(0xffffffffu, sb, o);
         dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
       }
       if (valid) {
-        const float pb = expf(sb * a.scale - ls);
+        const float pb = expf(sb * a.scale - ls[it]);
         const float dsb = pb * (dpb - di);
         if (sub == 0) k.dsb[row] = dsb;
 #pragma unroll

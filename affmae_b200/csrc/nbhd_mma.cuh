@@ -123,10 +123,11 @@ __device__ __forceinline__ void mma_chunk_pv(float (*out)[4], const uint32_t* a,
 
 // Scatter-add of R[16 x 32] = Pt[0..15][0..15]^T (16 x 16, row stride pst) *
 // Y[16 x 32] (times `mul`) into key rows 8 * uclu[u >> 3] + (u & 7), u = u0 + i,
-// of dst (fp32, row stride TD) for u < U.
+// of dst (fp32, row stride TD) for u < U and key rows below N (the partial
+// last cluster has no rows past the last token).
 template <typename T>
 __device__ __forceinline__ void mma_chunk_scatter(const T* Pt, int pst, const T* Y, const int* uclu, int U,
-                                                  int u0, float mul, float* __restrict__ dst) {
+                                                  int u0, float mul, float* __restrict__ dst, int N) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
   uint32_t a[4];
@@ -141,8 +142,10 @@ __device__ __forceinline__ void mma_chunk_scatter(const T* Pt, int pst, const T*
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     MmaType<T>::mma(acc, a, yb);
     const int col = nt * 8 + 2 * tq;
-    if (ua < U) red_add_v2(dst + ((int64_t)uclu[ua >> 3] * 8 + (ua & 7)) * TD + col, acc[0] * mul, acc[1] * mul);
-    if (ub < U) red_add_v2(dst + ((int64_t)uclu[ub >> 3] * 8 + (ub & 7)) * TD + col, acc[2] * mul, acc[3] * mul);
+    const int ka = ua < U ? uclu[ua >> 3] * 8 + (ua & 7) : N;
+    const int kb = ub < U ? uclu[ub >> 3] * 8 + (ub & 7) : N;
+    if (ka < N) red_add_v2(dst + (int64_t)ka * TD + col, acc[0] * mul, acc[1] * mul);
+    if (kb < N) red_add_v2(dst + (int64_t)kb * TD + col, acc[2] * mul, acc[3] * mul);
   }
 }
 

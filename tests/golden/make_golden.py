@@ -11,7 +11,8 @@ the reference package touches a GPU driver at import time:
 Launchers that assert ``is_cuda`` are bypassed by calling the next layer down
 (the launcher functions the asserting wrapper calls).
 
-Usage:  python tests/golden/make_golden.py [--reference /path/to/affmae]
+Usage:  python tests/golden/make_golden.py --reference /path/to/affmae
+        (or AFFMAE_REFERENCE=/path/to/affmae python tests/golden/make_golden.py)
 This needs the reference checkout and is only run when fixtures change; the
 tests read the committed .npz files.
 """
@@ -254,8 +255,11 @@ def gen_clusters(R):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
+                    help="checkout of najafian-lab/affmae (or set AFFMAE_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give the reference checkout with --reference or AFFMAE_REFERENCE")
     R = load_reference(a.reference)
     R["_root"] = a.reference
     torch.set_num_threads(1)

@@ -212,7 +212,7 @@ deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     Top4 top;
     grid_knn4(gv, b, sx, sy, top);
     reinterpret_cast<int4*>(knn_idx)[gs] = make_int4(top.i[0], top.i[1], top.i[2], top.i[3]);
-    reinterpret_cast<float4*>(knn_d2)[gs] = make_float4(top.d[0], top.d[1], top.d[2], top.d[3]);
+    if (knn_d2) reinterpret_cast<float4*>(knn_d2)[gs] = make_float4(top.d[0], top.d[1], top.d[2], top.d[3]);
     float w[4], dist[4];
     shepard4(top.d, P, w, dist);
 #pragma unroll
@@ -253,6 +253,26 @@ deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
   }
 }
 
+// Squared distances of sample gs to its 4 neighbours: the saved ones, or
+// (knn_d2 == NULL) recomputed from the positions with the forward's rounding
+// (sample = q + offset, then sqdist2), which reproduces them bit for bit.
+__device__ __forceinline__ void load_d2(const float* __restrict__ knn_d2, int64_t gs, int4 ii,
+                                        const float* __restrict__ kvb, float qx, float qy,
+                                        const float* __restrict__ offsets, float* d2) {
+  if (knn_d2) {
+    const float4 dd = reinterpret_cast<const float4*>(knn_d2)[gs];
+    d2[0] = dd.x; d2[1] = dd.y; d2[2] = dd.z; d2[3] = dd.w;
+    return;
+  }
+  const float sx = __fadd_rn(qx, offsets[2 * gs]);
+  const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
+  const int id[4] = {ii.x, ii.y, ii.z, ii.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    d2[j] = sqdist2(sx, sy, kvb[2 * (int64_t)id[j]], kvb[2 * (int64_t)id[j] + 1]);
+  }
+}
+
 // Backward, one warp per query.  Per head the 4 points x 4 neighbours give 16
 // (kv row, coefficient aw * w) entries; entries naming the same kv row are
 // merged first (neighbouring sampling points share neighbours), so each
@@ -289,11 +309,13 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
   for (int64_t gq = (int64_t)blockIdx.x * DK_WARPS + warp; gq < B * Nq;
        gq += (int64_t)gridDim.x * DK_WARPS) {
     const int64_t b = gq / Nq;
+    const float* kvb = kvpos + b * Nkv * 2;
+    const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
     for (int s = lane; s < S; s += 32) {
       const int64_t gs = gq * S + s;
       const int4 ii = reinterpret_cast<const int4*>(knn_idx)[gs];
-      const float4 dd = reinterpret_cast<const float4*>(knn_d2)[gs];
-      const float d2[4] = {dd.x, dd.y, dd.z, dd.w};
+      float d2[4];
+      load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
       s_idx[warp][s * 4 + 0] = ii.x; s_idx[warp][s * 4 + 1] = ii.y;
@@ -354,15 +376,15 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     for (int t = lane; t < S * 4; t += 32) { s_w[warp][t] = 0.f; s_cf[warp][t] = 0.f; }
     __syncwarp();
     float gqx = 0.f, gqy = 0.f;
-    const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
-    const float* kvb = kvpos + b * Nkv * 2;
     float* dkvb = d_kvpos + b * Nkv * 2;
     for (int s = lane; s < S; s += 32) {
       const int64_t gs = gq * S + s;
       const float sx = __fadd_rn(qx, offsets[2 * gs]);
       const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
-      const float4 dd = reinterpret_cast<const float4*>(knn_d2)[gs];
-      const float d2[4] = {dd.x, dd.y, dd.z, dd.w};
+      const int4 ii = make_int4(s_idx[warp][s * 4], s_idx[warp][s * 4 + 1], s_idx[warp][s * 4 + 2],
+                                s_idx[warp][s * 4 + 3]);
+      float d2[4];
+      load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
       const float aw = s_aw[warp][s];

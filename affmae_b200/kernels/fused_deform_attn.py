@@ -30,8 +30,12 @@ def workspace_bytes(B: int, Nkv: int) -> int:
 
 
 def fused_knn_deform_cross_attn_forward_save(query_pos, kv_pos, offsets, attn_weights, values,
-                                             power, D=2):
-    """Returns (out [B,Nq,H,C], knn_idx [B,Nq,H,4,4] int32, knn_dist_sq [B,Nq,H,4,4] fp32)."""
+                                             power, D=2, save_dist=True):
+    """Returns (out [B,Nq,H,C], knn_idx [B,Nq,H,4,4] int32, knn_dist_sq [B,Nq,H,4,4] fp32).
+
+    ``save_dist=False`` (used by the autograd Functions) skips writing the
+    squared distances and returns None for them; the backward recomputes them
+    from the positions bit for bit."""
     assert D == 2, "Currently only D=2 is supported"
     B, Nq, _ = query_pos.shape
     Nkv = kv_pos.shape[1]
@@ -46,7 +50,7 @@ def fused_knn_deform_cross_attn_forward_save(query_pos, kv_pos, offsets, attn_we
     pw = nat.scalar_dev(power, dev)
     out = torch.empty((B, Nq, H, C), device=dev, dtype=values.dtype)
     knn_idx = torch.empty((B, Nq, H, K, 4), device=dev, dtype=torch.int32)
-    knn_d2 = torch.empty((B, Nq, H, K, 4), device=dev, dtype=torch.float32)
+    knn_d2 = torch.empty((B, Nq, H, K, 4), device=dev, dtype=torch.float32) if save_dist else None
     ws = torch.empty(workspace_bytes(B, Nkv), device=dev, dtype=torch.uint8)
     nat.call("affb_deform_knn_fwd", nat.ptr(qp), nat.ptr(kp), nat.ptr(off), nat.ptr(aw),
              nat.ptr(val), nat.ptr(pw), nat.dcode(val), B, Nq, Nkv, H, C, nat.ptr(out),
@@ -54,8 +58,8 @@ def fused_knn_deform_cross_attn_forward_save(query_pos, kv_pos, offsets, attn_we
     return out, knn_idx, knn_d2
 
 
-def fused_knn_deform_self_attn_forward_save(pos, offsets, attn_weights, values, power, D=2):
-    return fused_knn_deform_cross_attn_forward_save(pos, pos, offsets, attn_weights, values, power, D)
+def fused_knn_deform_self_attn_forward_save(pos, offsets, attn_weights, values, power, D=2, save_dist=True):
+    return fused_knn_deform_cross_attn_forward_save(pos, pos, offsets, attn_weights, values, power, D, save_dist)
 
 
 def _deform_backward(dout, query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx,
@@ -78,7 +82,7 @@ def _deform_backward(dout, query_pos, kv_pos, offsets, attn_weights, values, pow
     d_pow = torch.zeros((1,), device=dev, dtype=torch.float32)
     nat.call("affb_deform_knn_bwd", nat.ptr(qp), nat.ptr(kp), nat.ptr(off), nat.ptr(aw),
              nat.ptr(val), nat.ptr(pw), nat.ptr(knn_idx.contiguous()),
-             nat.ptr(knn_dist_sq.contiguous()), nat.ptr(g), nat.dcode(val), B, Nq, Nkv, H, C,
+             nat.ptr(None if knn_dist_sq is None else knn_dist_sq.contiguous()), nat.ptr(g), nat.dcode(val), B, Nq, Nkv, H, C,
              nat.ptr(d_off), nat.ptr(d_aw), nat.ptr(d_qpos), nat.ptr(d_kvpos), nat.ptr(d_val),
              nat.ptr(d_pow), nat.stream(dev))
     return d_qpos, d_kvpos, d_off, d_aw, nat.cast_from_f32(d_val, values.dtype), d_pow
@@ -113,17 +117,17 @@ class FusedKNNDeformSelfAttnFunction(Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, pos, offsets, attn_weights, values, power, D=2):
-        out, knn_idx, knn_d2 = fused_knn_deform_self_attn_forward_save(
-            pos, offsets, attn_weights, values, power, D)
-        ctx.save_for_backward(pos, offsets, attn_weights, values, power, knn_idx, knn_d2)
+        out, knn_idx, _ = fused_knn_deform_self_attn_forward_save(
+            pos, offsets, attn_weights, values, power, D, save_dist=False)
+        ctx.save_for_backward(pos, offsets, attn_weights, values, power, knn_idx)
         return out
 
     @staticmethod
     @custom_bwd(device_type="cuda")
     def backward(ctx, dout):
-        pos, offsets, attn_weights, values, power, knn_idx, knn_d2 = ctx.saved_tensors
+        pos, offsets, attn_weights, values, power, knn_idx = ctx.saved_tensors
         dpos, doff, daw, dval, dpow = fused_knn_deform_self_attn_backward(
-            dout, pos, offsets, attn_weights, values, power, knn_idx, knn_d2)
+            dout, pos, offsets, attn_weights, values, power, knn_idx, None)
         return dpos, doff, daw, dval, _power_grad(dpow, power), None
 
 
@@ -131,18 +135,17 @@ class FusedKNNDeformCrossAttnFunction(Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, query_pos, kv_pos, offsets, attn_weights, values, power, D=2):
-        out, knn_idx, knn_d2 = fused_knn_deform_cross_attn_forward_save(
-            query_pos, kv_pos, offsets, attn_weights, values, power, D)
-        ctx.save_for_backward(query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx,
-                              knn_d2)
+        out, knn_idx, _ = fused_knn_deform_cross_attn_forward_save(
+            query_pos, kv_pos, offsets, attn_weights, values, power, D, save_dist=False)
+        ctx.save_for_backward(query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx)
         return out
 
     @staticmethod
     @custom_bwd(device_type="cuda")
     def backward(ctx, dout):
-        query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx, knn_d2 = ctx.saved_tensors
+        query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx = ctx.saved_tensors
         dq, dkv, doff, daw, dval, dpow = fused_knn_deform_cross_attn_backward(
-            dout, query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx, knn_d2)
+            dout, query_pos, kv_pos, offsets, attn_weights, values, power, knn_idx, None)
         return dq, dkv, doff, daw, dval, _power_grad(dpow, power), None
 
 

@@ -14,6 +14,10 @@ GB/s; the same command under ``ncu -k <kernel>`` gives the kernel profiles.
   wfeat      config 5 stage-1 merging: weights [16,13107,48,4], feat [16,32768,96] bf16, fwd+bwd
   wfeat-fwd  the same, forward only
   wgather    config 1: idx [2,1024,48], softmax weights, feat [2,4096,128] fp32, fwd+bwd
+  layer-norm  config 5 stage 1: residual + dropout + LayerNorm, 524288 rows of 96, fwd+bwd
+  rel-bias    config 5 stage 1: in-kernel relative-position bias [16,3,32768,48], fwd+bwd
+  head-layout config 5 stage 1: kv head split + output merge, [16,32768,3x32], fwd+bwd
+  deform-nbidx  deformable attention with given 4-NN indices (non-fused path), fwd+bwd
 
 Algorithmic bytes count every interface tensor once (inputs read, outputs
 written), as the roofline of a gather-bound operator.
@@ -154,10 +158,96 @@ def op_wgather():
     return step, fwd + bwd, {"B": B, "M": Mq, "K": K, "N": N, "C": C, "dtype": "fp32", "pass": "fwd+bwd"}
 
 
+def op_layer_norm():
+    """Config 5 stage 1: LayerNorm(x + dropout(delta)) over 16 x 32768 tokens of C=96,
+    fp32 residual stream and bf16 delta, fp32 + bf16 outputs, fwd+bwd."""
+    from .kernels.layer_norm import fused_layer_norm
+    g = torch.Generator().manual_seed(0)
+    R, C = 16 * 32768, 96
+    x = torch.randn((R, C), generator=g).to("cuda").requires_grad_(True)
+    d = torch.randn((R, C), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
+    w = torch.ones(C, device="cuda", requires_grad=True)
+    b = torch.zeros(C, device="cuda", requires_grad=True)
+    g32 = torch.randn((R, C), generator=g).to("cuda")
+    g16 = torch.randn((R, C), generator=g).to("cuda", torch.bfloat16)
+
+    def step():
+        y32, y16 = fused_layer_norm(x, w, b, 1e-5, delta=d, p=0.1, out32=True, out16=True)
+        torch.autograd.backward((y32, y16), (g32, g16))
+    # fwd: x, delta in; s (saved sum), y32, y16 out; bwd: g32, g16, s in; dx, ddelta out
+    fwd = R * C * (4 + 2 + 4 + 4 + 2)
+    bwd = R * C * (4 + 2 + 4 + 4 + 2)
+    return step, fwd + bwd, {"rows": R, "C": C, "x": "fp32", "delta": "bf16", "p": 0.1, "pass": "fwd+bwd"}
+
+
+def op_rel_bias():
+    """Config 5 stage 1 relative-position bias: pe_idx [16,32768,48], H=3, bf16 out, fwd+bwd."""
+    from .kernels.pos_bias import rel_pos_bias
+    g = torch.Generator().manual_seed(0)
+    B, N, M, H = 16, 32768, 48, 3
+    pe = (torch.randint(110, 145, (B, N, M), generator=g) * 255 + torch.randint(110, 145, (B, N, M), generator=g))
+    pe = pe.to("cuda")
+    w = (0.02 * torch.randn((H, 5), generator=g)).to("cuda").requires_grad_(True)
+    bb = torch.zeros(H, device="cuda", requires_grad=True)
+    dout = torch.randn((B, H, N, M), generator=g).to("cuda", torch.bfloat16)
+
+    def step():
+        rel_pos_bias(w, bb, pe, torch.bfloat16).backward(dout)
+    fwd = B * N * M * 8 + B * H * N * M * 2
+    bwd = B * N * M * 8 + B * H * N * M * 2
+    return step, fwd + bwd, {"B": B, "N": N, "M": M, "H": H, "pass": "fwd+bwd"}
+
+
+def op_head_layout():
+    """ClusterAttention head split of a [16, 32768, 2 x 3 x 32] kv projection and the merge
+    of the output, bf16, fwd+bwd."""
+    from .kernels.head_layout import merge_heads, split_heads
+    g = torch.Generator().manual_seed(0)
+    B, N, H, d = 16, 32768, 3, 32
+    x = torch.randn((B, N, 2 * H * d), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
+    gk = torch.randn((B, H, N, d), generator=g).to("cuda", torch.bfloat16)
+
+    def step():
+        k, v = split_heads(x, H, 2)
+        y = merge_heads(k)
+        torch.autograd.backward([y, v], [gk.permute(0, 2, 1, 3).reshape(B, N, H * d), gk])
+    el = B * N * H * d * 2
+    return step, 2 * (2 * el * 2 + el * 2), {"B": B, "N": N, "H": H, "d": d, "pass": "split+merge fwd+bwd"}
+
+
+def op_deform_nbidx():
+    """The reference's non-fused deformable path (attention.py:339-358): 4-NN indices given,
+    [B*H, Nq*4] samples over one 96^2 kv level, C=32 bf16 (config 4 level 0), fwd+bwd."""
+    from .kernels.fused_deform_attn import FusedDeformAttnFunction
+    g = torch.Generator().manual_seed(0)
+    BH, S, Nkv, C = 16 * 8, 9216 * 4, 9216, 32
+    ii = torch.arange(96).float()
+    ys, xs = torch.meshgrid(ii, ii, indexing="ij")
+    kv = torch.stack([xs, ys], -1).reshape(1, -1, 2).expand(BH, -1, -1).contiguous()
+    sl = torch.rand((BH, S, 2), generator=g) * 96 - 0.5
+    nb = (sl.round().clamp(0, 95)[..., 1:2] * 96 + sl.round().clamp(0, 95)[..., 0:1]).long()
+    nb = torch.cat([nb, (nb + 1) % Nkv, (nb + 96) % Nkv, (nb + 97) % Nkv], -1)
+    aw = torch.rand((BH, S), generator=g)
+    val = torch.randn((BH, Nkv, C), generator=g)
+    dout = torch.randn((BH, S, C), generator=g).to("cuda", torch.bfloat16)
+    leaves = [t.to("cuda").requires_grad_(True) for t in (sl, kv)]
+    awc = aw.to("cuda").requires_grad_(True)
+    vc = val.to("cuda", torch.bfloat16).requires_grad_(True)
+    nbc = nb.to("cuda").int()
+    power = torch.tensor(1.0, device="cuda", requires_grad=True)
+
+    def step():
+        FusedDeformAttnFunction.apply(leaves[0], leaves[1], nbc, power, awc, vc, 2, None).backward(dout)
+    fwd = _nbytes(sl, kv, nbc, aw) + _nbytes(vc, dout)
+    bwd = _nbytes(dout, sl, kv, nbc, aw, vc) + _nbytes(sl, kv, aw, vc)
+    return step, fwd + bwd, {"BH": BH, "samples": S, "Nkv": Nkv, "C": C, "pass": "fwd+bwd"}
+
+
 OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_deform, "deform-mae": op_deform_mae,
        "deform-mae-raster": lambda: op_deform_mae(raster=True), "wfeat": op_wfeat,
        "wfeat-fwd": lambda: op_wfeat(fwd_only=True),
-       "wgather": op_wgather}
+       "wgather": op_wgather, "layer-norm": op_layer_norm, "rel-bias": op_rel_bias,
+       "head-layout": op_head_layout, "deform-nbidx": op_deform_nbidx}
 
 
 def main():

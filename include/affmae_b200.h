@@ -175,7 +175,7 @@ int affb_dropout_keep_mask(uint32_t seed, float p, int64_t e0, int64_t n, uint8_
  * softmax(-P*(sqrt(d2)+1e-6)) with +1e-8 in the denominator;
  * out [B,Nq,H,C] T = sum_p attn_w * sum_j w_j v_j.
  * knn_idx [B,Nq,H,4,4] int32 and knn_d2 [B,Nq,H,4,4] fp32 are written for the
- * backward.  `workspace` (device, affb_deform_workspace_bytes(B,Nkv) bytes,
+ * backward (knn_d2 may be NULL: not written).  `workspace` (device, affb_deform_workspace_bytes(B,Nkv) bytes,
  * 256-byte aligned) receives the spatial grid of kv_pos built by this call. */
 int64_t affb_deform_workspace_bytes(int64_t B, int64_t Nkv);
 int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos, const float* offsets,
@@ -215,7 +215,9 @@ int affb_deform_knn_fwd_noalloc(const float* query_pos, const float* kv_pos,
  * Written: d_offsets [B,Nq,H,4,2] fp32, d_attn_w [B,Nq,H,4] fp32.
  * Accumulated (zeroed by the caller): d_qpos [B,Nq,2] fp32,
  * d_kvpos [B,Nkv,2] fp32 (may alias d_qpos for self-attention),
- * d_values_acc [B,Nkv,H,C] fp32, d_power [1] fp32.                          */
+ * d_values_acc [B,Nkv,H,C] fp32, d_power [1] fp32.  knn_d2 may be NULL: the
+ * squared distances are then recomputed from the positions with the
+ * forward's rounding (the same values bit for bit).                        */
 int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos, const float* offsets,
                         const float* attn_w, const void* values, const float* power,
                         const int32_t* knn_idx, const float* knn_d2, const void* dout,

@@ -666,3 +666,21 @@ def test_head_split_merge(cuda, dtype, parts):
     gy = torch.randn(y.shape, generator=gen).to(cuda, dtype)
     y.backward(gy)
     assert torch.equal(o.grad, gy.view(B, N, H, d).permute(0, 2, 1, 3))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_deform_backward_recomputes_distances(cuda, dtype):
+    """The autograd path saves only the neighbour indices: the backward given
+    knn_d2 = None recomputes the squared distances and returns the same
+    gradients, bit for bit, as the backward given the saved distances."""
+    from affmae_b200.kernels.fused_deform_attn import (fused_knn_deform_cross_attn_forward_save,
+                                                       fused_knn_deform_cross_attn_backward)
+    qp, kv, off, aw, val, power, do = _deform_inputs(2, 300, 40, 8, 32, dtype, seed=9)
+    args = [t.to(cuda) for t in (qp, kv, off, aw, val, power)]
+    _, ki, kd = fused_knn_deform_cross_attn_forward_save(*args)
+    _, ki2, none = fused_knn_deform_cross_attn_forward_save(*args, save_dist=False)
+    assert none is None and torch.equal(ki, ki2)
+    g1 = fused_knn_deform_cross_attn_backward(do.to(cuda), *args, ki, kd)
+    g2 = fused_knn_deform_cross_attn_backward(do.to(cuda), *args, ki, None)
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)

@@ -42,6 +42,7 @@ from .kernels.knn import knn
 from .kernels.layer_norm import FusedLayerNorm
 from .kernels.local_attn import FlashLocalAttentionFunction
 from .kernels.pos_bias import pos_bias_gather, rel_pos_bias
+from .kernels.token_mask import apply_token_mask
 from .kernels.weighted_features import weighted_features
 from .workloads import REL_POS_WIDTH, TABLE_WIDTH, relative_position_table
 
@@ -323,8 +324,7 @@ class PatchEmbed(nn.Module):
         x = x.contiguous(memory_format=torch.channels_last)
         for i, conv in enumerate(self.convs):
             x = conv(x)
-            scale = max(self.patch_size >> (i + 1), 1)
-            x = x * token_mask.to(x.dtype).repeat_interleave(scale, 1).repeat_interleave(scale, 2)[:, None]
+            x = apply_token_mask(x, token_mask)
             if i < len(self.norms):
                 y = self.norms[i](x.permute(0, 2, 3, 1), out32=False, out16=True)
                 x = F.gelu(y).permute(0, 3, 1, 2)
@@ -552,8 +552,7 @@ class AFFMaskedAutoEncoder(nn.Module):
         token_mask = torch.ones((B, L), device=imgs.device)
         token_mask.scatter_(1, ids_masked, 0.0)
         token_mask = token_mask.view(B, H // p, W // p)
-        pixel_mask = token_mask.repeat_interleave(p, 1).repeat_interleave(p, 2)[:, None]
-        pos, feat, h, w = self.encoder.patch_embed(imgs * pixel_mask, token_mask)
+        pos, feat, h, w = self.encoder.patch_embed(apply_token_mask(imgs, token_mask), token_mask)
         C0 = feat.shape[-1]
         vis_feat = feat.gather(1, ids_keep[..., None].expand(-1, -1, C0))
         vis_pos = pos.gather(1, ids_keep[..., None].expand(-1, -1, 2))

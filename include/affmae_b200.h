@@ -163,6 +163,15 @@ int affb_layer_norm_bwd(const float* dy32, const void* dy16_bf16, const void* s,
  * of the model glue; the reference uses torch's dropout here.              */
 int affb_dropout_keep_mask(uint32_t seed, float p, int64_t e0, int64_t n, uint8_t* keep);
 
+/* Token-mask multiply of the masked-autoencoder patch stem: the re-masking
+ * after each stride-2 convolution of AFFPatchEmbed (src/layers/aff.py:591-639)
+ * without materialising the upsampled mask.  x, out [B,h,w,C] T
+ * (channels-last), token_mask [B,th,tw] uint8 (nonzero = keep), h/th = w/tw
+ * an integer s: out[b,y,x,c] = x[b,y,x,c] * token_mask[b,y/s,x/s].  Also the
+ * gradient (the same product).                                              */
+int affb_token_mask_apply(const void* x, int dtype, int64_t B, int64_t h, int64_t w, int64_t C,
+                          const uint8_t* token_mask, int64_t th, int64_t tw, void* out, void* stream);
+
 /* --------------------------------- fused KNN deformable attention (2-D) --
  * Replaces fused_knn_deform_cross_attn_forward_save
  * (src/layers/kernels/fused_deform_attn.py:2592) and, with kv_pos == query_pos

@@ -1,0 +1,131 @@
+"""Generate module-level golden vectors from the reference's own layer modules.
+
+Runs the reference's unchanged ``ClusterAttention``,
+``DeformableCrossAttention`` and ``DeformableSelfAttention``
+(src/layers/attention.py:20-207, :210-404, :407-593) on the CPU with their
+Triton kernels under ``TRITON_INTERPRET=1``, with seeded random parameters
+and inputs, and stores parameters, inputs, outputs and every gradient in
+``tests/golden/module_*.npz``.  ``tests/test_module_parity.py`` loads the same
+parameters into this package's modules (affmae_b200.mae) and compares on the
+GPU.  The reference's ``src/layers/kernels/util.py`` queries a GPU driver at
+import and is replaced by a stub; the reference packages' ``__init__`` files
+are skipped.
+
+Usage:  python tests/golden/make_module_golden.py --reference /path/to/affmae
+        (or AFFMAE_REFERENCE=/path/to/affmae python tests/golden/make_module_golden.py)
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import types
+from pathlib import Path
+
+os.environ["TRITON_INTERPRET"] = "1"
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+
+
+def load_attention(root: str):
+    def pkg(name, path):
+        m = types.ModuleType(name)
+        m.__path__ = [path]
+        sys.modules[name] = m
+    pkg("src", f"{root}/src")
+    pkg("src.layers", f"{root}/src/layers")
+    pkg("src.layers.kernels", f"{root}/src/layers/kernels")
+    pkg("src.utils", f"{root}/src/utils")
+    util = types.ModuleType("src.layers.kernels.util")
+    util.NUM_STAGES_OPTIONS = [1, 2]
+    util.is_hip = lambda: False
+    util.is_cuda = lambda: True
+    util.supports_host_descriptor = lambda: False
+    sys.modules["src.layers.kernels.util"] = util
+    import src.layers.attention as attention  # noqa: E402
+    return attention
+
+
+def randomise(module: torch.nn.Module, g: torch.Generator, std: float = 0.2):
+    """Every parameter drawn N(0, std) (the zero initialisations of the offset
+    and weight projections would leave their gradients untested)."""
+    with torch.no_grad():
+        for p in module.parameters():
+            p.copy_(torch.randn(p.shape, generator=g) * std)
+
+
+def save(name, module, **arrays):
+    out = {f"param.{k}": v.detach().numpy() for k, v in module.named_parameters()}
+    out.update({f"grad.{k}": v.grad.detach().numpy() for k, v in module.named_parameters() if v.grad is not None})
+    out.update({k: (v.detach().numpy() if torch.is_tensor(v) else np.asarray(v)) for k, v in arrays.items()})
+    np.savez_compressed(HERE / f"module_{name}.npz", **out)
+    print(f"  wrote module_{name}.npz", flush=True)
+
+
+def gen_cluster_attention(A):
+    """64 tokens on an 8x8 grid in row order, clusters of 8 consecutive tokens,
+    each token attending the 6 clusters with the nearest means (48 keys),
+    relative-position indices as in BasicLayer.forward (aff.py:426-465)."""
+    g = torch.Generator().manual_seed(11)
+    m = A.ClusterAttention(64, 2)
+    randomise(m, g)
+    N, M = 64, 48
+    ys, xs = torch.meshgrid(torch.arange(8.0), torch.arange(8.0), indexing="ij")
+    pos = torch.stack([xs, ys], -1).reshape(1, N, 2)
+    means = pos.view(1, 8, 8, 2).mean(2)
+    d = ((pos[:, :, None] - means[:, None]) ** 2).sum(-1)
+    near = torch.sort(d, dim=-1, stable=True)[1][..., :6]
+    member = (near[..., None] * 8 + torch.arange(8)).reshape(1, N, M)
+    nb = pos[0][member[0]][None]
+    rel = (nb - (pos[:, :, None] - 127)).clamp(0, 254).long()
+    pe_idx = rel[..., 1] * 255 + rel[..., 0]
+    feat = torch.randn((1, N, 64), generator=g).requires_grad_(True)
+    dout = torch.randn((1, N, 64), generator=g)
+    out = m(feat, member, None, pe_idx, False)
+    out.backward(dout)
+    save("cluster_attention", m, feat=feat, member=member, pe_idx=pe_idx, dout=dout, out=out,
+         d_feat=feat.grad, dim=64, heads=2)
+
+
+def gen_deformable(A, cls, name):
+    g = torch.Generator().manual_seed(12 if cls is A.DeformableCrossAttention else 13)
+    m = cls(64, 2, 4)
+    randomise(m, g)
+    with torch.no_grad():
+        m.shepard_power.fill_(1.3)
+    Nq, Nkv = 24, 40
+    query = torch.randn((1, Nq, 64), generator=g).requires_grad_(True)
+    qpos = torch.rand((1, Nq, 2), generator=g) * 8
+    dout = torch.randn((1, Nq, 64), generator=g)
+    if cls is A.DeformableCrossAttention:
+        kv = torch.randn((1, Nkv, 64), generator=g).requires_grad_(True)
+        kpos = torch.rand((1, Nkv, 2), generator=g) * 8
+        out = m(query, qpos, kv, kpos)
+        out.backward(dout)
+        save(name, m, query=query, query_pos=qpos, kv=kv, kv_pos=kpos, dout=dout, out=out, d_query=query.grad,
+             d_kv=kv.grad, dim=64, heads=2)
+    else:
+        out = m(query, qpos)
+        out.backward(dout)
+        save(name, m, query=query, query_pos=qpos, dout=dout, out=out, d_query=query.grad, dim=64, heads=2)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
+                    help="checkout of najafian-lab/affmae (or set AFFMAE_REFERENCE)")
+    a = ap.parse_args()
+    if not a.reference:
+        ap.error("give the reference checkout with --reference or AFFMAE_REFERENCE")
+    torch.set_num_threads(1)
+    A = load_attention(a.reference)
+    gen_cluster_attention(A)
+    gen_deformable(A, A.DeformableCrossAttention, "deform_cross")
+    gen_deformable(A, A.DeformableSelfAttention, "deform_self")
+
+
+if __name__ == "__main__":
+    main()

@@ -672,7 +672,7 @@ def test_head_split_merge(cuda, dtype, parts):
 def test_deform_backward_recomputes_distances(cuda, dtype):
     """The autograd path saves only the neighbour indices: the backward given
     knn_d2 = None recomputes the squared distances and returns the same
-    gradients, bit for bit, as the backward given the saved distances."""
+    gradients as the backward given the saved distances."""
     from affmae_b200.kernels.fused_deform_attn import (fused_knn_deform_cross_attn_forward_save,
                                                        fused_knn_deform_cross_attn_backward)
     qp, kv, off, aw, val, power, do = _deform_inputs(2, 300, 40, 8, 32, dtype, seed=9)
@@ -682,5 +682,10 @@ def test_deform_backward_recomputes_distances(cuda, dtype):
     assert none is None and torch.equal(ki, ki2)
     g1 = fused_knn_deform_cross_attn_backward(do.to(cuda), *args, ki, kd)
     g2 = fused_knn_deform_cross_attn_backward(do.to(cuda), *args, ki, None)
-    for a, b in zip(g1, g2):
-        assert torch.equal(a, b)
+    # per-sample gradients are written once: bit-exact; the scatter-added ones
+    # (atomics, order not fixed) within fp32 summation-order error
+    for name, a, b in zip(["d_qpos", "d_kvpos", "d_off", "d_aw", "d_val", "d_power"], g1, g2):
+        if name in ("d_off", "d_aw"):
+            assert torch.equal(a, b), name
+        else:
+            assert rel_err(a.float().cpu(), b.float().cpu()) < (1e-5 if dtype == torch.float32 else 1e-2), name

@@ -172,3 +172,23 @@ def test_mae_ddp_two_gpus_matches_single_gpu(cuda, tmp_path):
         den += float(g.pow(2).sum())
         assert torch.isfinite(ddp[n]).all(), n
     assert (num / den) ** 0.5 < 2e-2, (num / den) ** 0.5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("C,scale,dtype", [(1, 4, torch.float32), (48, 2, torch.bfloat16), (96, 1, torch.bfloat16),
+                                           (12, 2, torch.float32)])
+def test_token_mask_matches_upsampled_multiply(cuda, C, scale, dtype):
+    """The patch stem's re-masking kernel equals x * repeat_interleave(mask)
+    bit for bit, forward and gradient (reference aff.py:591-639)."""
+    from affmae_b200.kernels.token_mask import apply_token_mask
+    g = torch.Generator().manual_seed(C)
+    B, th, tw = 2, 16, 16
+    tm = (torch.rand((B, th, tw), generator=g) > 0.5).float().to(cuda)
+    x = torch.randn((B, C, th * scale, tw * scale), generator=g).to(cuda, dtype)
+    x = x.contiguous(memory_format=torch.channels_last).requires_grad_(True)
+    up = tm.repeat_interleave(scale, 1).repeat_interleave(scale, 2)[:, None].to(dtype)
+    out = apply_token_mask(x, tm)
+    assert torch.equal(out, x.detach() * up)
+    gy = torch.randn(out.shape, generator=g).to(cuda, dtype)
+    (gx,) = torch.autograd.grad(out, x, gy)
+    assert torch.equal(gx, gy * up)

@@ -49,6 +49,10 @@ METRIC = "nbr-attn fwd+bwd HBM GB/s"
 # inverse-list kernels, the query-side and the key-side kernel
 LAUNCHES_PER_STEP = 6
 CFG = dict(B=32, side=96, keep=0.5, H=4, d=32, nbhd=48)
+# DRAM bytes (read + write) of one backward call per image, from one ncu capture of
+# every backward kernel at B=16 (profiles/nbhd_attn_kernels_config3_b16.md: 291.1 MB);
+# the traffic of each kernel grows with the batch, so it is scaled by B
+BWD_DRAM_BYTES_PER_IMAGE = 291.113216e6 / 16
 
 
 def workload_config(extra=None):
@@ -382,7 +386,9 @@ def run_gpu(args, world, rank, local):
                     "value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_s * 1e3 / args.steps},
                 "roofline": {"kernel": "affb_nbhd_attn_bwd (list, query-side and key-side kernels)", "bound": "hbm", "achieved": achieved, "peak": peak,
-                             "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                             "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                             "traffic": BWD_DRAM_BYTES_PER_IMAGE * CFG["B"],
+                             "traffic_note": "ncu dram__bytes_read+write of the backward kernels at B=16, scaled by B",
                              "algorithmic_bytes": bwd_bytes, "kernel_ms": kbwd},
                 "cpu_baseline": cpu, "clocks": clocks,
                 "gpu_launches": args.steps * LAUNCHES_PER_STEP}

@@ -63,6 +63,7 @@ SIGNATURES = {
     "affb_mssample_bwd": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p],
     "affb_cast_f32": [_p, _p, _i32, _i64, _p],
     "affb_dropout_keep_mask": [_u32, _f32, _i64, _i64, _p],
+    "affb_nbhd_build": [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p],
     "affb_token_mask_apply": [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p],
 }
 OTHER_SYMBOLS = ["affb_last_error", "affb_abi_version", "affb_deform_workspace_bytes",

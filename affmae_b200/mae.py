@@ -35,6 +35,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _native as nat
 from .kernels.fused_deform_attn import (fused_knn_deformable_cross_attention,
                                         fused_knn_deformable_self_attention)
 from .kernels.head_layout import merge_heads, split_heads
@@ -122,18 +123,22 @@ def curve_clusters(pos: torch.Tensor, m: int, h: int, w: int):
 
 
 def neighbourhood(pos: torch.Tensor, means: torch.Tensor, cmask, nbhd: int, m: int):
-    """member_idx [B,n,M] (int64, padding slots -> 0), mask [B,n,M] bool or
-    None, pe_idx [B,n,M] for tokens in cluster order (aff.py:426-465)."""
+    """member_idx [B,n,M] (int32, padding slots -> 0), mask [B,n,M] bool or
+    None, pe_idx [B,n,M] int64 for tokens in cluster order (aff.py:426-465):
+    the nearest-cluster search on the KNN kernel, then one kernel that expands
+    the cluster ids into the three lists."""
     B, n, _ = pos.shape
     k = means.shape[1]
     nnc = min(int(round(nbhd / m)), k)
-    nearest = knn(pos, means, nnc)                                       # [B,n,nnc]
-    raw = (nearest[..., None] * m + torch.arange(m, device=pos.device)).reshape(B, n, nnc * m)
-    member = torch.where(raw < n, raw, torch.zeros_like(raw))
-    mask = (raw < n) if cmask is not None else None
-    nb = pos.gather(1, member.reshape(B, -1, 1).expand(-1, -1, 2)).reshape(B, n, nnc * m, 2)
-    rel = (nb - (pos[:, :, None] - REL_POS_WIDTH)).clamp(0, TABLE_WIDTH - 1)
-    pe_idx = (rel[..., 1] * TABLE_WIDTH + rel[..., 0]).long()
+    assert m == 8, "the neighbour-list kernel expands clusters of 8 tokens"
+    nearest = knn(pos, means, nnc).contiguous()                          # [B,n,nnc] int64
+    M = nnc * m
+    p = pos.float().contiguous()
+    member = torch.empty((B, n, M), device=pos.device, dtype=torch.int32)
+    pe_idx = torch.empty((B, n, M), device=pos.device, dtype=torch.int64)
+    mask = torch.empty((B, n, M), device=pos.device, dtype=torch.bool) if cmask is not None else None
+    nat.call("affb_nbhd_build", nat.ptr(p), nat.ptr(nearest), B, n, nnc, nat.ptr(member),
+             nat.ptr(mask.view(torch.uint8)) if mask is not None else None, nat.ptr(pe_idx), nat.stream(pos.device))
     return member, mask, pe_idx
 
 
@@ -258,7 +263,7 @@ class ClusterMerging(nn.Module):
         sel = idx[..., None].expand(-1, -1, M)
         member = member_idx.gather(1, sel)
         pe = pe_idx.gather(1, sel)
-        lp = importance.gather(1, member.reshape(B, -1, 1)).reshape(B, keep, M, 1)
+        lp = importance.gather(1, member.reshape(B, -1, 1).long()).reshape(B, keep, M, 1)
         if mask is not None:
             lp = lp * mask.gather(1, sel)[..., None]
         table = self.weight_net(self.rel_table.to(feat.dtype))           # [T, inner]

@@ -400,8 +400,8 @@ def run_mae(args, world, rank, local, steps=None, warmup=None):
     """Config 5: AFF-small MAE pretraining steps, data parallel over `world`
     GPUs (DDP, NCCL all-reduce overlapped with the backward pass).  Returns
     the JSON line on rank 0 (None elsewhere)."""
-    steps = steps if steps is None else steps
-    warmup = warmup if warmup is None else warmup
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     from affmae_b200 import _native as nat
     from affmae_b200.mae import MAEConfig
     from affmae_b200.pretrain import build, synthetic_images, train_step

@@ -163,6 +163,17 @@ int affb_layer_norm_bwd(const float* dy32, const void* dy16_bf16, const void* s,
  * of the model glue; the reference uses torch's dropout here.              */
 int affb_dropout_keep_mask(uint32_t seed, float p, int64_t e0, int64_t n, uint8_t* keep);
 
+/* Neighbour lists of an encoder stage (BasicLayer.forward,
+ * src/layers/aff.py:426-465) from the ids of every token's nnc nearest
+ * clusters: pos [B,n,2] fp32 in cluster order (clusters of 8 consecutive
+ * tokens), nearest [B,n,nnc] int64 (e.g. from affb_knn2d against the cluster
+ * means).  Writes member_idx [B,n,8 nnc] int32 (8c+r, or 0 past the last
+ * token), mask [B,n,8 nnc] uint8 (8c+r < n; NULL to skip) and pe_idx
+ * [B,n,8 nnc] int64 = y*255 + x of clamp(pos[member] - pos[q] + 127, 0, 254),
+ * with the fp32 rounding of the reference's PyTorch sequence.               */
+int affb_nbhd_build(const float* pos, const int64_t* nearest, int64_t B, int64_t n, int64_t nnc,
+                    int32_t* member_idx, uint8_t* mask, int64_t* pe_idx, void* stream);
+
 /* Token-mask multiply of the masked-autoencoder patch stem: the re-masking
  * after each stride-2 convolution of AFFPatchEmbed (src/layers/aff.py:591-639)
  * without materialising the upsampled mask.  x, out [B,h,w,C] T

@@ -94,7 +94,8 @@ def test_neighbourhood_on_gpu_matches_exact_knn(cuda):
     near = torch.sort(d, dim=-1, stable=True)[1][..., :6]
     raw = (near[..., None] * 8 + torch.arange(8)).reshape(*near.shape[:2], 48)
     n = pos.shape[1]
-    assert torch.equal(member.cpu(), torch.where(raw < n, raw, torch.zeros_like(raw)))
+    assert member.dtype == torch.int32
+    assert torch.equal(member.cpu().long(), torch.where(raw < n, raw, torch.zeros_like(raw)))
     assert torch.equal(mask.cpu(), raw < n)
     nb = pos.cpu()[torch.arange(2)[:, None, None], member.cpu()]
     rel = (nb - (pos.cpu()[:, :, None] - REL_POS_WIDTH)).clamp(0, TABLE_WIDTH - 1)
@@ -192,3 +193,33 @@ def test_token_mask_matches_upsampled_multiply(cuda, C, scale, dtype):
     gy = torch.randn(out.shape, generator=g).to(cuda, dtype)
     (gx,) = torch.autograd.grad(out, x, gy)
     assert torch.equal(gx, gy * up)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [1021, 1024])
+def test_neighbour_list_kernel_matches_torch_sequence(cuda, n):
+    """The neighbour-list kernel equals the reference's PyTorch sequence
+    (aff.py:445-465: expand the nearest clusters, zero the padding, gather the
+    positions, clamp the offsets, index the table) bit for bit, also for
+    positions off the integer grid (the stage-4 tokens of a merged stage)."""
+    from affmae_b200.mae import neighbourhood
+    from affmae_b200.workloads import REL_POS_WIDTH, TABLE_WIDTH
+    g = torch.Generator().manual_seed(n)
+    pos = (torch.rand((2, n, 2), generator=g) * 180).to(cuda)
+    k = (n + 7) // 8
+    means = (torch.rand((2, k, 2), generator=g) * 180).to(cuda)
+    cmask = torch.ones((2, k, 8), device=cuda) if n % 8 else None
+    member, mask, pe = neighbourhood(pos, means, cmask, 48, 8)
+    from affmae_b200.kernels.knn import knn
+    nearest = knn(pos, means, 6)
+    raw = (nearest[..., None] * 8 + torch.arange(8, device=cuda)).reshape(2, n, 48)
+    ref_member = torch.where(raw < n, raw, torch.zeros_like(raw))
+    nb = pos.gather(1, ref_member.reshape(2, -1, 1).expand(-1, -1, 2)).reshape(2, n, 48, 2)
+    rel = (nb - (pos[:, :, None] - REL_POS_WIDTH)).clamp(0, TABLE_WIDTH - 1)
+    ref_pe = (rel[..., 1] * TABLE_WIDTH + rel[..., 0]).long()
+    assert torch.equal(member.long(), ref_member)
+    assert torch.equal(pe, ref_pe)
+    if n % 8:
+        assert torch.equal(mask, raw < n)
+    else:
+        assert mask is None

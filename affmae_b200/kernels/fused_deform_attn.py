@@ -226,3 +226,37 @@ def fused_deformable_attention(sampling_locs, kv_pos, nb_idx, power, attn_weight
     values [B,Nkv,C] -> [B,N,C]."""
     return FusedDeformAttnFunction.apply(sampling_locs, kv_pos, nb_idx, power, attn_weights,
                                          values, D, use_heuristics)
+
+
+# ------------------------------------------- public helpers of the reference
+USE_HEURISTICS = True
+
+
+def set_use_heuristics(value: bool):
+    """The reference's switch between autotuning and launch heuristics
+    (fused_deform_attn.py:721).  These kernels have fixed launch shapes; the
+    flag is kept for callers that set it and has no effect."""
+    global USE_HEURISTICS
+    USE_HEURISTICS = bool(value)
+
+
+def fused_knn_deform_self_attn_forward(pos, offsets, attn_weights, values, power, D=2, use_heuristics=True):
+    """Forward only (fused_deform_attn.py:2387): out [B,N,H,C], nothing saved."""
+    out, _, _ = fused_knn_deform_cross_attn_forward_save(pos, pos, offsets, attn_weights, values, power, D,
+                                                         save_dist=False)
+    return out
+
+
+def fused_knn_deform_cross_attn_forward(query_pos, kv_pos, offsets, attn_weights, values, power, D=2,
+                                        use_heuristics=True):
+    """Forward only (fused_deform_attn.py:2460): out [B,Nq,H,C], nothing saved."""
+    out, _, _ = fused_knn_deform_cross_attn_forward_save(query_pos, kv_pos, offsets, attn_weights, values, power,
+                                                         D, save_dist=False)
+    return out
+
+
+def compute_softmax_weights(knn_dist_sq, power):
+    """The reference's helper over saved squared distances
+    (fused_deform_attn.py:3608): softmax_j(-max(power, 1e-6) * d2_j)."""
+    p = torch.clamp(power, min=1e-6)
+    return torch.softmax(-p * knn_dist_sq, dim=-1)

@@ -91,3 +91,17 @@ def knn(query, database, k, return_dist=False, D=None):
         distances = ((query.unsqueeze(2) - nbr) ** 2).sum(dim=-1)
         return indices, distances
     return indices
+
+
+def knn_pytorch_large(query, ref, k):
+    """Same contract as the reference's cdist + topk path (knn.py:1312): int64
+    indices [B, M, k] of the k nearest ``ref`` points, here from the exact
+    kernel (ties by lower index; the reference's topk leaves their order open)."""
+    D = query.shape[-1]
+    _check(query, ref, k, D)
+    return _knn_int64(query, ref, k, D)
+
+
+def knn_large_k_fallback(query, ref, k):
+    """The reference's large-K entry (knn.py:1336); the same exact kernel."""
+    return knn_pytorch_large(query, ref, k)

@@ -73,3 +73,14 @@ def weighted_features_ref(weights, feat, nbhd_idx):
     gathered = feat.gather(dim=1, index=nbhd_idx.reshape(B, N_out * M)[..., None].expand(-1, -1, C))
     gathered = gathered.reshape(B, N_out, M, C)
     return (weights[..., None] * gathered[:, :, :, None, :]).sum(dim=2)
+
+
+def weighted_features_triton(weights, feat, nbhd_idx):
+    """Forward launcher of the reference (weighted_features.py:114): [B,No,IC,C]."""
+    return weighted_features_fwd(weights, feat, nbhd_idx)
+
+
+def weighted_features_triton_backward(dout, weights, feat, nbhd_idx):
+    """Backward launcher of the reference (weighted_features.py:348): (d_weights, d_feat)."""
+    dw, dfeat = weighted_features_bwd(dout, weights, feat, nbhd_idx)
+    return dw.to(weights.dtype), dfeat.to(feat.dtype)

@@ -689,3 +689,28 @@ def test_deform_backward_recomputes_distances(cuda, dtype):
             assert torch.equal(a, b), name
         else:
             assert rel_err(a.float().cpu(), b.float().cpu()) < (1e-5 if dtype == torch.float32 else 1e-2), name
+
+
+def test_reference_public_helpers(cuda):
+    """The reference modules' remaining public helpers exist with their
+    signatures and agree with the main entry points."""
+    from affmae_b200.kernels import fused_deform_attn as fd, knn as kn, weighted_features as wf
+    gen = torch.Generator().manual_seed(3)
+    q = (torch.rand((2, 100, 2), generator=gen) * 20).to(cuda)
+    r = (torch.rand((2, 400, 2), generator=gen) * 20).to(cuda)
+    assert torch.equal(kn.knn_pytorch_large(q, r, 12), kn.knn(q, r, 12))
+    assert torch.equal(kn.knn_large_k_fallback(q, r, 40), oracle.knn(q.cpu(), r.cpu(), 40).to(cuda))
+    w = torch.randn((2, 30, 48, 4), generator=gen).to(cuda)
+    f = torch.randn((2, 100, 32), generator=gen).to(cuda)
+    idx = torch.randint(0, 100, (2, 30, 48), generator=gen).to(cuda)
+    assert torch.equal(wf.weighted_features_triton(w, f, idx), wf.weighted_features_fwd(w, f, idx))
+    dw, df = wf.weighted_features_triton_backward(torch.ones((2, 30, 4, 32), device=cuda), w, f, idx)
+    assert dw.shape == w.shape and df.shape == f.shape
+    qp, kv, off, aw, val, power, _ = _deform_inputs(1, 64, 12, 2, 16, torch.float32, seed=2)
+    args = [t.to(cuda) for t in (qp, kv, off, aw, val, power)]
+    out, _, d2 = fd.fused_knn_deform_cross_attn_forward_save(*args)
+    assert torch.equal(fd.fused_knn_deform_cross_attn_forward(*args), out)
+    sw = fd.compute_softmax_weights(d2, args[-1])
+    assert torch.allclose(sw.sum(-1), torch.ones_like(sw.sum(-1)))
+    fd.set_use_heuristics(False)
+    fd.set_use_heuristics(True)

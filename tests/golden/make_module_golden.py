@@ -2,7 +2,8 @@
 
 Runs the reference's unchanged ``ClusterAttention``,
 ``DeformableCrossAttention`` and ``DeformableSelfAttention``
-(src/layers/attention.py:20-207, :210-404, :407-593) on the CPU with their
+(src/layers/attention.py:20-207, :210-404, :407-593) and ``ClusterMerging``
+(src/layers/aff.py:120-299) on the CPU with their
 Triton kernels under ``TRITON_INTERPRET=1``, with seeded random parameters
 and inputs, and stores parameters, inputs, outputs and every gradient in
 ``tests/golden/module_*.npz``.  ``tests/test_module_parity.py`` loads the same
@@ -45,6 +46,19 @@ def load_attention(root: str):
     util.is_cuda = lambda: True
     util.supports_host_descriptor = lambda: False
     sys.modules["src.layers.kernels.util"] = util
+    # third-party imports of aff.py / geometry.py that the modules used here do
+    # not call: pykeops (absent here) and timm's DropPath / trunc_normal_
+    sys.modules.setdefault("pykeops", types.ModuleType("pykeops"))
+    pk = types.ModuleType("pykeops.torch")
+    pk.LazyTensor = None
+    sys.modules.setdefault("pykeops.torch", pk)
+    if "timm" not in sys.modules:
+        layers = types.ModuleType("timm.models.layers")
+        layers.DropPath = lambda p=0.0: torch.nn.Identity()
+        layers.trunc_normal_ = torch.nn.init.trunc_normal_
+        for name, mod in [("timm", types.ModuleType("timm")), ("timm.models", types.ModuleType("timm.models")),
+                          ("timm.models.layers", layers)]:
+            sys.modules[name] = mod
     import src.layers.attention as attention  # noqa: E402
     return attention
 
@@ -113,6 +127,54 @@ def gen_deformable(A, cls, name):
         save(name, m, query=query, query_pos=qpos, dout=dout, out=out, d_query=query.grad, dim=64, heads=2)
 
 
+def gen_cluster_merging(A, root):
+    """ClusterMerging (aff.py:120-299) with the model's settings (cluster
+    merging, no reserve tokens, ds_rate 0.4).  Its weighted_features wrapper
+    asserts CUDA tensors (weighted_features.py:411), so the reference's own
+    launchers one layer down (weighted_features_triton and its backward) are
+    bound into an autograd Function for this CPU run."""
+    import importlib
+    aff = importlib.import_module("src.layers.aff")
+    wf = importlib.import_module("src.layers.kernels.weighted_features")
+
+    class WF(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, w, f, idx):
+            ctx.save_for_backward(w, f, idx)
+            return wf.weighted_features_triton(w, f, idx.to(torch.int32))
+
+        @staticmethod
+        def backward(ctx, dout):
+            w, f, idx = ctx.saved_tensors
+            dw, df = wf.weighted_features_triton_backward(dout.contiguous(), w, f, idx.to(torch.int32))
+            return dw, df, None
+
+    aff.weighted_features = WF.apply
+    g = torch.Generator().manual_seed(14)
+    m = aff.ClusterMerging(64, 96, ds_rate=0.4, reserve_on=False)
+    randomise(m, g)
+    with torch.no_grad():
+        m.weight_net[1].weight.add_(1.0)
+        m.norm.weight.add_(1.0)
+    n, M = 80, 48
+    ys, xs = torch.meshgrid(torch.arange(8.0), torch.arange(10.0), indexing="ij")
+    pos = (torch.stack([xs, ys], -1).reshape(1, n, 2) * 2)
+    means = pos.view(1, n // 8, 8, 2).mean(2)
+    d = ((pos[:, :, None] - means[:, None]) ** 2).sum(-1)
+    near = torch.sort(d, dim=-1, stable=True)[1][..., :6]
+    member = (near[..., None] * 8 + torch.arange(8)).reshape(1, n, M)
+    nb = pos[0][member[0]][None]
+    rel = (nb - (pos[:, :, None] - 127)).clamp(0, 254).long()
+    pe_idx = rel[..., 1] * 255 + rel[..., 0]
+    feat = torch.randn((1, n, 64), generator=g).requires_grad_(True)
+    prob = torch.sigmoid(torch.randn((1, n, 1), generator=g)).requires_grad_(True)
+    pos_down, feat_down = m(pos, feat, member, None, prob, 2, pe_idx, 0)
+    dout = torch.randn(feat_down.shape, generator=g)
+    feat_down.backward(dout)
+    save("cluster_merging", m, pos=pos, feat=feat, member=member, pe_idx=pe_idx, prob=prob, pos_down=pos_down,
+         feat_down=feat_down, dout=dout, d_feat=feat.grad, d_prob=prob.grad, dim=64, out_dim=96, ds_rate=0.4)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
@@ -125,6 +187,7 @@ def main():
     gen_cluster_attention(A)
     gen_deformable(A, A.DeformableCrossAttention, "deform_cross")
     gen_deformable(A, A.DeformableSelfAttention, "deform_self")
+    gen_cluster_merging(A, a.reference)
 
 
 if __name__ == "__main__":

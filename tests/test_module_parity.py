@@ -22,8 +22,9 @@ import torch
 from conftest import golden, rel_err
 
 
-def _load(module, g, cuda):
-    params = {k[len("param."):]: v for k, v in g.items() if k.startswith("param.")}
+def _load(module, g, cuda, unused=()):
+    params = {k[len("param."):]: v for k, v in g.items() if k.startswith("param.") and
+              not k[len("param."):].startswith(unused)}
     missing, unexpected = module.load_state_dict(params, strict=False)
     assert not unexpected, unexpected
     assert not [k for k in missing if k in dict(module.named_parameters())], missing
@@ -35,6 +36,8 @@ LOOSE = {"pos_embed.bias": 1.5e-2}
 
 def _grads_match(module, g, tol):
     for name, p in module.named_parameters():
+        if p.grad is None and "grad." + name not in g:
+            continue
         ref = g.get("grad." + name)
         assert ref is not None, name
         assert rel_err(p.grad.cpu(), ref) < max(tol, LOOSE.get(name, 0.0)), name
@@ -101,4 +104,30 @@ def test_deformable_attention_matches_reference_module(cuda, tag):
     assert rel_err(query.grad.cpu(), g["d_query"]) < 1e-4
     if tag == "deform_cross":
         assert rel_err(kv.grad.cpu(), g["d_kv"]) < 1e-4
+    _grads_match(m, g, 1e-4)
+
+
+@pytest.mark.gpu
+def test_cluster_merging_matches_reference_module(cuda):
+    """ClusterMerging (aff.py:120-299, the model's settings: no reserve tokens,
+    ds_rate 0.4).  The kept tokens come from an unsorted top-k, whose order is
+    left open, so outputs are matched by position.  The reference's
+    global_norm / global_linear serve a path without neighbour lists and are
+    not created here."""
+    from affmae_b200.mae import ClusterMerging
+    g = golden("module_cluster_merging")
+    m = _load(ClusterMerging(int(g["dim"]), int(g["out_dim"]), float(g["ds_rate"])), g, cuda, unused=("global_",))
+    feat = g["feat"].to(cuda).requires_grad_(True)
+    prob = g["prob"].to(cuda).requires_grad_(True)
+    pos_down, feat_down = m(g["pos"].to(cuda), feat, g["member"].to(cuda), None, prob, g["pe_idx"].to(cuda))
+    key = lambda p: (p[..., 1] * 100000 + p[..., 0]).reshape(-1)
+    ours = torch.argsort(key(pos_down.detach().cpu()))
+    ref = torch.argsort(key(g["pos_down"]))
+    assert torch.equal(pos_down.detach().cpu()[0, ours], g["pos_down"][0, ref])
+    assert rel_err(feat_down.detach().cpu()[0, ours], g["feat_down"][0, ref]) < 1e-4
+    dout = torch.empty_like(g["dout"])
+    dout[0, ours] = g["dout"][0, ref]
+    feat_down.backward(dout.to(cuda))
+    assert rel_err(feat.grad.cpu(), g["d_feat"]) < 1e-4
+    assert rel_err(prob.grad.cpu(), g["d_prob"]) < 1e-4
     _grads_match(m, g, 1e-4)

@@ -175,6 +175,40 @@ def gen_cluster_merging(A, root):
          feat_down=feat_down, dout=dout, d_feat=feat.grad, d_prob=prob.grad, dim=64, out_dim=96, ds_rate=0.4)
 
 
+def gen_stage(A, root):
+    """One encoder stage, BasicLayer (aff.py:330-510): space-filling clustering,
+    nearest-cluster neighbourhoods, two ClusterTransformerBlocks and
+    ClusterMerging, on 102 tokens in a 16x16 canvas (a partial last cluster).
+    The stage's KNN wrapper asserts CUDA tensors (knn.py:1384); it is bound to
+    the oracle's exact KNN (the reference kernel's (distance, index) order,
+    pinned by the KNN golden vectors) for this CPU run."""
+    import importlib
+    sys.path.insert(0, str(HERE.parent.parent))
+    import oracle
+    aff = importlib.import_module("src.layers.aff")
+    aff.triton_knn = lambda q, r, k, **kw: oracle.knn(q, r, k)
+    g = torch.Generator().manual_seed(15)
+    m = aff.BasicLayer(64, 96, cluster_size=8, nbhd_size=48, depth=2, num_heads=2, mlp_ratio=2.0, ds_rate=0.4,
+                       downsample=aff.ClusterMerging)
+    randomise(m, g)
+    with torch.no_grad():
+        for mod in m.modules():
+            if isinstance(mod, torch.nn.LayerNorm):
+                mod.weight.add_(1.0)
+    n = 102
+    # positions off the grid: the clustering sorts a key in which symmetric
+    # grid positions can tie, and the order of ties is left to the sort
+    # implementation (it differs between devices in the reference as well)
+    pos = torch.rand((1, n, 2), generator=g) * 16
+    feat = torch.randn((1, n, 64), generator=g).requires_grad_(True)
+    pos_o, feat_o, pos_down, feat_down = m(pos, feat, 16, 16, False, 2)
+    d_o = torch.randn(feat_o.shape, generator=g)
+    d_down = torch.randn(feat_down.shape, generator=g)
+    torch.autograd.backward([feat_o, feat_down], [d_o, d_down])
+    save("stage", m, pos=pos, feat=feat, pos_out=pos_o, feat_out=feat_o, pos_down=pos_down, feat_down=feat_down,
+         d_out=d_o, d_down=d_down, d_feat=feat.grad, dim=64, out_dim=96, heads=2, depth=2, hw=16)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
@@ -188,6 +222,7 @@ def main():
     gen_deformable(A, A.DeformableCrossAttention, "deform_cross")
     gen_deformable(A, A.DeformableSelfAttention, "deform_self")
     gen_cluster_merging(A, a.reference)
+    gen_stage(A, a.reference)
 
 
 if __name__ == "__main__":

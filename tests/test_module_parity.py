@@ -131,3 +131,53 @@ def test_cluster_merging_matches_reference_module(cuda):
     assert rel_err(feat.grad.cpu(), g["d_feat"]) < 1e-4
     assert rel_err(prob.grad.cpu(), g["d_prob"]) < 1e-4
     _grads_match(m, g, 1e-4)
+
+
+def _stage_name(ref: str) -> str:
+    """Reference BasicLayer parameter name -> affmae_b200.mae.Stage name."""
+    return ref.replace(".mlp.fc", ".fc").replace("downsample.", "merge.")
+
+
+@pytest.mark.gpu
+def test_stage_matches_reference_basic_layer(cuda):
+    """A whole encoder stage against the reference's BasicLayer (aff.py:330-510):
+    space-filling clustering, nearest-cluster neighbourhoods and relative
+    indices, two cluster-attention blocks and cluster merging, on 102 tokens
+    (a partial last cluster) in a 16x16 canvas."""
+    from affmae_b200.mae import MAEConfig, Stage
+    g = golden("module_stage")
+    cfg = MAEConfig(drop_path_rate=0.0)
+    m = Stage(int(g["dim"]), int(g["out_dim"]), int(g["depth"]), int(g["heads"]), cfg, [0.0] * int(g["depth"]))
+    params = {_stage_name(k[6:]): v for k, v in g.items() if k.startswith("param.") and ".global_" not in k}
+    missing, unexpected = m.load_state_dict(params, strict=False)
+    assert not unexpected, unexpected
+    assert not [k for k in missing if k in dict(m.named_parameters())], missing
+    m = m.to(cuda)
+    feat = g["feat"].to(cuda).requires_grad_(True)
+    hw = int(g["hw"])
+    pos_o, feat_o, pos_down, feat_down = m(g["pos"].to(cuda), feat, hw, hw)
+    assert torch.equal(pos_o.cpu(), g["pos_out"])
+    assert rel_err(feat_o.detach().cpu(), g["feat_out"]) < 2e-3
+    key = lambda p: (p[..., 1] * 100000 + p[..., 0]).reshape(-1)
+    ours = torch.argsort(key(pos_down.detach().cpu()))
+    ref = torch.argsort(key(g["pos_down"]))
+    assert torch.equal(pos_down.detach().cpu()[0, ours], g["pos_down"][0, ref])
+    assert rel_err(feat_down.detach().cpu()[0, ours], g["feat_down"][0, ref]) < 2e-3
+    d_down = torch.empty_like(g["d_down"])
+    d_down[0, ours] = g["d_down"][0, ref]
+    torch.autograd.backward([feat_o, feat_down], [g["d_out"].to(cuda), d_down.to(cuda)])
+    assert rel_err(feat.grad.cpu(), g["d_feat"]) < 2e-3
+    for ref_name in [k[5:] for k in g if k.startswith("grad.") and ".global_" not in k]:
+        p = dict(m.named_parameters())[_stage_name(ref_name)]
+        if ref_name.endswith("pos_embed.bias"):
+            # sum of dS over every (query, neighbour) pair: per row it cancels to
+            # -dS of the blank token, so the exact value is near zero and the
+            # reference's fp16 rounding of O dominates it; compared absolutely,
+            # on the scale of the same Linear's weight gradient
+            wref = g["grad." + ref_name[:-len("bias")] + "weight"]
+            err = (p.grad.cpu().double() - g["grad." + ref_name].double()).abs().max().item()
+            assert err < 1.5e-2 * wref.abs().max().item(), ref_name
+            continue
+        # the position-bias Linear sums dS over all pairs (see the module docstring)
+        tol = 1.5e-2 if ".pos_embed." in ref_name else 2e-3
+        assert rel_err(p.grad.cpu(), g["grad." + ref_name]) < tol, ref_name

@@ -463,11 +463,18 @@ class DecoderBlock(nn.Module):
         """q: fp32 residual stream; q16: the same values in the autocast dtype
         (the Linears' input).  Each norm(q + dropout(delta)) is one fused pass
         returning both."""
-        q, q16 = self.norm1(q, self.self_attn(q16, q_pos), self.p, out32=True, out16=True)
-        q, q16 = self.norm2(q, self.cross_attn(q16, q_pos, src + src_embed, src_pos), self.p,
-                            out32=True, out16=True)
+        q, q16 = self._norm(self.norm1, q, self.self_attn(q16, q_pos))
+        q, q16 = self._norm(self.norm2, q, self.cross_attn(q16, q_pos, src + src_embed, src_pos))
         ff = self.linear2(self.drop(F.relu(self.linear1(q16))))
-        return self.norm3(q, ff, self.p, out32=True, out16=True)
+        return self._norm(self.norm3, q, ff)
+
+    def _norm(self, norm, q, delta):
+        """(fp32 residual stream, Linear input): a bf16 copy under autocast,
+        the fp32 values themselves outside it."""
+        if q.is_cuda and torch.is_autocast_enabled("cuda"):
+            return norm(q, delta, self.p, out32=True, out16=True)
+        y = norm(q, delta, self.p, out32=True)
+        return y, y
 
 
 class PixelDecoder(nn.Module):

@@ -3,7 +3,8 @@
 Runs the reference's unchanged ``ClusterAttention``,
 ``DeformableCrossAttention`` and ``DeformableSelfAttention``
 (src/layers/attention.py:20-207, :210-404, :407-593) and ``ClusterMerging``
-(src/layers/aff.py:120-299) on the CPU with their
+(src/layers/aff.py:120-299), BasicLayer (aff.py:330-510) and MSDecoderBlock
+(src/layers/decoder.py:73-143) on the CPU with their
 Triton kernels under ``TRITON_INTERPRET=1``, with seeded random parameters
 and inputs, and stores parameters, inputs, outputs and every gradient in
 ``tests/golden/module_*.npz``.  ``tests/test_module_parity.py`` loads the same
@@ -46,7 +47,7 @@ def load_attention(root: str):
     util.is_cuda = lambda: True
     util.supports_host_descriptor = lambda: False
     sys.modules["src.layers.kernels.util"] = util
-    # third-party imports of aff.py / geometry.py that the modules used here do
+    # third-party imports of aff.py / geometry.py / decoder.py that the modules used here do
     # not call: pykeops (absent here) and timm's DropPath / trunc_normal_
     sys.modules.setdefault("pykeops", types.ModuleType("pykeops"))
     pk = types.ModuleType("pykeops.torch")
@@ -59,6 +60,10 @@ def load_attention(root: str):
         for name, mod in [("timm", types.ModuleType("timm")), ("timm.models", types.ModuleType("timm.models")),
                           ("timm.models.layers", layers)]:
             sys.modules[name] = mod
+    if "fvcore" not in sys.modules:  # imported by decoder.py, unused by its blocks
+        for name in ("fvcore", "fvcore.nn", "fvcore.nn.weight_init"):
+            sys.modules[name] = types.ModuleType(name)
+        sys.modules["fvcore.nn"].weight_init = sys.modules["fvcore.nn.weight_init"]
     import src.layers.attention as attention  # noqa: E402
     return attention
 
@@ -209,6 +214,34 @@ def gen_stage(A, root):
          d_out=d_o, d_down=d_down, d_feat=feat.grad, dim=64, out_dim=96, heads=2, depth=2, hw=16)
 
 
+def gen_decoder_block(root):
+    """One decoder block, MSDecoderBlock (decoder.py:73-143): deformable
+    self-attention, deformable cross-attention into encoder features with
+    their position embedding, ReLU FFN, post-norm residuals; no dropout."""
+    import importlib
+    dec = importlib.import_module("src.layers.decoder")
+    g = torch.Generator().manual_seed(16)
+    m = dec.MSDecoderBlock(d_model=64, n_heads=2, n_points=4, d_ffn=128, dropout=0.0)
+    randomise(m, g)
+    with torch.no_grad():
+        for mod in m.modules():
+            if isinstance(mod, torch.nn.LayerNorm):
+                mod.weight.add_(1.0)
+        for att in (m.self_attn, m.cross_attn):
+            att.shepard_power.fill_(1.2)
+    Nq, Ns = 24, 40
+    query = torch.randn((1, Nq, 64), generator=g).requires_grad_(True)
+    qpos = torch.rand((1, Nq, 2), generator=g) * 8
+    src = torch.randn((1, Ns, 64), generator=g).requires_grad_(True)
+    spos = torch.rand((1, Ns, 2), generator=g) * 8
+    embed = torch.randn((1, Ns, 64), generator=g) * 0.5
+    out = m(query, qpos, src, spos, embed)
+    dout = torch.randn(out.shape, generator=g)
+    out.backward(dout)
+    save("decoder_block", m, query=query, query_pos=qpos, src=src, src_pos=spos, src_embed=embed, out=out,
+         dout=dout, d_query=query.grad, d_src=src.grad, dim=64, heads=2, ffn=128)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
@@ -223,6 +256,7 @@ def main():
     gen_deformable(A, A.DeformableSelfAttention, "deform_self")
     gen_cluster_merging(A, a.reference)
     gen_stage(A, a.reference)
+    gen_decoder_block(a.reference)
 
 
 if __name__ == "__main__":

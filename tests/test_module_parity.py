@@ -181,3 +181,20 @@ def test_stage_matches_reference_basic_layer(cuda):
         # the position-bias Linear sums dS over all pairs (see the module docstring)
         tol = 1.5e-2 if ".pos_embed." in ref_name else 2e-3
         assert rel_err(p.grad.cpu(), g["grad." + ref_name]) < tol, ref_name
+
+
+@pytest.mark.gpu
+def test_decoder_block_matches_reference_block(cuda):
+    """One decoder block against the reference's MSDecoderBlock
+    (decoder.py:73-143), in fp32 at 1e-4."""
+    from affmae_b200.mae import DecoderBlock
+    g = golden("module_decoder_block")
+    m = _load(DecoderBlock(int(g["dim"]), int(g["heads"]), int(g["ffn"]), 0.0), g, cuda)
+    q = g["query"].to(cuda).requires_grad_(True)
+    src = g["src"].to(cuda).requires_grad_(True)
+    out, _ = m(q, q, g["query_pos"].to(cuda), src, g["src_pos"].to(cuda), g["src_embed"].to(cuda))
+    assert rel_err(out.detach().cpu(), g["out"]) < 1e-4
+    out.backward(g["dout"].to(cuda))
+    assert rel_err(q.grad.cpu(), g["d_query"]) < 1e-4
+    assert rel_err(src.grad.cpu(), g["d_src"]) < 1e-4
+    _grads_match(m, g, 1e-4)

@@ -29,6 +29,7 @@ on the host cores on a bounded sample (one image per step).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -445,6 +446,33 @@ def run_mae(args, world, rank, local, steps=None, warmup=None):
         e3.record(stream)
         torch.cuda.synchronize()
         e2e_s = max_over_ranks(e2.elapsed_time(e3) / 1e3, world)
+        # exposed gradient all-reduce: forward + backward with DDP's bucketed
+        # all-reduce against the same under no_sync() (no collective), CUDA events,
+        # max over ranks
+        split = None
+        if world > 1:
+            def fb(sync):
+                with contextlib.nullcontext() if sync else model.no_sync():
+                    with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                        l, _ = model(imgs, generator=gen)
+                    l.backward()
+                opt.zero_grad(set_to_none=True)
+            ms = {}
+            for sync in (True, False):
+                fb(sync)
+                torch.cuda.synchronize()
+                barrier(world)
+                a = torch.cuda.Event(enable_timing=True)
+                c = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(max(1, min(steps, 5))):
+                    fb(sync)
+                c.record(stream)
+                torch.cuda.synchronize()
+                ms[sync] = max_over_ranks(a.elapsed_time(c) / max(1, min(steps, 5)), world)
+            split = {"fwd_bwd_ms_with_allreduce": ms[True], "fwd_bwd_ms_without_allreduce": ms[False],
+                     "allreduce_exposed_ms": ms[True] - ms[False],
+                     "collective": "NCCL all-reduce of fp32 gradients in DDP buckets, overlapped with backward"}
     clocks = clk.summary()
     if rank == 0:
         value = world * per_gpu * steps / dev_s
@@ -462,7 +490,7 @@ def run_mae(args, world, rank, local, steps=None, warmup=None):
                         "ms_per_step": e2e_s * 1e3 / steps},
                 "roofline": None, "cpu_baseline": None,
                 "cpu_baseline_note": "not run for config 5 (a CPU pretraining step is infeasible)",
-                "clocks": clocks, "abi_calls_per_step": calls / steps}
+                "clocks": clocks, "abi_calls_per_step": calls / steps, "ddp_split": split}
         return line
     return None
 
@@ -512,7 +540,7 @@ def main():
                                "ms_per_step": m["ms_per_step"], "steps": m["steps"], "warmup": m["warmup"],
                                "per_gpu_batch": m["config"]["per_gpu_batch"],
                                "parallelism": m["config"]["parallelism"], "e2e_img_per_s": m["e2e"]["value"],
-                               "final_loss": m["final_loss"], "clocks": m["clocks"],
+                               "final_loss": m["final_loss"], "clocks": m["clocks"], "ddp_split": m["ddp_split"],
                                "workload": m["config"]["workload"]}
         if line is not None:
             print(json.dumps(line), flush=True)

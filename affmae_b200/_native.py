@@ -63,12 +63,16 @@ SIGNATURES = {
     "affb_mssample_bwd": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p],
     "affb_cast_f32": [_p, _p, _i32, _i64, _p],
     "affb_dropout_keep_mask": [_u32, _f32, _i64, _i64, _p],
+    "affb_nbhd_attn_fwd_plan": [_p, _p, _p, _p, _p, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _f32,
+                                _p, _p, _p, _i64, _p],
+    "affb_nbhd_attn_bwd_plan": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i64,
+                                _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _p],
     "affb_nbhd_build": [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p],
     "affb_token_mask_apply": [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p],
 }
 OTHER_SYMBOLS = ["affb_last_error", "affb_abi_version", "affb_deform_workspace_bytes",
                  "affb_deform_noalloc_max_scratch_bytes", "affb_nbhd_attn_bwd_workspace_bytes",
-                 "affb_knn2d_workspace_bytes"]
+                 "affb_knn2d_workspace_bytes", "affb_nbhd_tile_plan_bytes"]
 
 
 def library_path() -> Path:
@@ -100,6 +104,8 @@ def lib():
         l.affb_nbhd_attn_bwd_workspace_bytes.argtypes = [_i32, _i64, _i64, _i64, _i64, _i64]
         l.affb_knn2d_workspace_bytes.restype = C.c_int64
         l.affb_knn2d_workspace_bytes.argtypes = [_i64, _i64]
+        l.affb_nbhd_tile_plan_bytes.restype = C.c_int64
+        l.affb_nbhd_tile_plan_bytes.argtypes = [_i32, _i64, _i64, _i64, _i64]
         for name, args in SIGNATURES.items():
             fn = getattr(l, name)
             fn.argtypes = args

@@ -87,17 +87,23 @@ static NbhdArgs make_args(const void* q, const void* k, const void* v, const int
 
 using namespace affb;
 
-extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
-                                  const int32_t* member_idx, const void* bias,
-                                  const uint8_t* mask, int mask_heads, const void* blank_k,
-                                  const void* blank_v, int dtype, int64_t B, int64_t H,
-                                  int64_t N, int64_t D, int64_t M, float scale, void* out,
-                                  float* lse, void* stream) {
+static int nbhd_fwd_impl(const void* q, const void* k, const void* v, const int32_t* member_idx, const void* bias,
+                         const uint8_t* mask, int mask_heads, const void* blank_k, const void* blank_v, int dtype,
+                         int64_t B, int64_t H, int64_t N, int64_t D, int64_t M, float scale, void* out, float* lse,
+                         void* tile_plan, int64_t tile_plan_bytes, void* stream) {
   if (int e = check_na(B, H, N, D, M, mask ? mask_heads : 1, blank_k, blank_v, q, k, v)) return e;
+  if (tile_plan) {
+    AFFB_REQUIRE(nbhd_tc_supported(dtype, D, M), "nbhd_attn_fwd: a tile plan needs the tensor-core path "
+                 "(bf16 / fp16, head_dim 32, at most 64 neighbours)");
+    AFFB_REQUIRE(tile_plan_bytes >= nbhd_tile_plan_bytes(B, N, M) && ((uintptr_t)tile_plan & 15) == 0,
+                 "nbhd_attn_fwd: tile plan of %lld bytes, %lld needed (16-byte aligned)", (long long)tile_plan_bytes,
+                 (long long)nbhd_tile_plan_bytes(B, N, M));
+  }
   if (B == 0 || N == 0) return AFFB_OK;
   NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, B, H, N, D, M, scale);
   a.out = out;
   a.lse = lse;
+  a.tile_plan = tile_plan;
   cudaStream_t st = as_stream(stream);
   if (nbhd_tc_supported(dtype, D, M)) {
     if (int e = nbhd_blk_fwd(a, dtype, (int)B, st)) return e;
@@ -109,6 +115,30 @@ extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
   }
   AFFB_LAUNCH_CHECK("affb_nbhd_attn_fwd");
   return AFFB_OK;
+}
+
+extern "C" int affb_nbhd_attn_fwd(const void* q, const void* k, const void* v,
+                                  const int32_t* member_idx, const void* bias,
+                                  const uint8_t* mask, int mask_heads, const void* blank_k,
+                                  const void* blank_v, int dtype, int64_t B, int64_t H,
+                                  int64_t N, int64_t D, int64_t M, float scale, void* out,
+                                  float* lse, void* stream) {
+  return nbhd_fwd_impl(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, dtype, B, H, N, D, M, scale,
+                       out, lse, nullptr, 0, stream);
+}
+
+extern "C" int64_t affb_nbhd_tile_plan_bytes(int dtype, int64_t B, int64_t N, int64_t D, int64_t M) {
+  if (B < 0 || N < 0 || M < 0) return -1;
+  return nbhd_tc_supported(dtype, D, M) ? nbhd_tile_plan_bytes(B, N, M) : 0;
+}
+
+extern "C" int affb_nbhd_attn_fwd_plan(const void* q, const void* k, const void* v, const int32_t* member_idx,
+                                       const void* bias, const uint8_t* mask, int mask_heads, const void* blank_k,
+                                       const void* blank_v, int dtype, int64_t B, int64_t H, int64_t N, int64_t D,
+                                       int64_t M, float scale, void* out, float* lse, void* tile_plan,
+                                       int64_t tile_plan_bytes, void* stream) {
+  return nbhd_fwd_impl(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, dtype, B, H, N, D, M, scale,
+                       out, lse, tile_plan, tile_plan_bytes, stream);
 }
 
 // fp32 runs the CUDA-core kernels straight into dk / dv; everything else
@@ -125,15 +155,12 @@ extern "C" int64_t affb_nbhd_attn_bwd_workspace_bytes(int dtype, int64_t B, int6
   return (int64_t)bwd_layout(dtype, B, H, N, D, M, nullptr).total;
 }
 
-extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* o,
-                                  const void* dout, const float* lse,
-                                  const int32_t* member_idx, const void* bias,
-                                  const uint8_t* mask, int mask_heads, const void* blank_k,
-                                  const void* blank_v, int dtype, int64_t B, int64_t H,
-                                  int64_t N, int64_t D, int64_t M, float scale, void* dq,
-                                  void* dk, void* dv, void* dbias, float* dbk_acc,
-                                  float* dbv_acc, void* workspace, int64_t workspace_bytes,
-                                  void* stream) {
+static int nbhd_bwd_impl(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                         const float* lse, const int32_t* member_idx, const void* bias, const uint8_t* mask,
+                         int mask_heads, const void* blank_k, const void* blank_v, int dtype, int64_t B, int64_t H,
+                         int64_t N, int64_t D, int64_t M, float scale, void* dq, void* dk, void* dv, void* dbias,
+                         float* dbk_acc, float* dbv_acc, const void* tile_plan, int64_t tile_plan_bytes,
+                         void* workspace, int64_t workspace_bytes, void* stream) {
   if (int e = check_na(B, H, N, D, M, mask ? mask_heads : 1, blank_k, blank_v, q, k, v)) return e;
   AFFB_REQUIRE(!blank_k || (dbk_acc && dbv_acc), "nbhd_attn_bwd: blank gradients need dbk/dbv buffers");
   AFFB_REQUIRE(!bias || dbias, "nbhd_attn_bwd: bias given without a dbias buffer");
@@ -146,6 +173,10 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
                "nbhd_attn_bwd: workspace of %lld bytes, %lld needed (affb_nbhd_attn_bwd_workspace_bytes)",
                (long long)workspace_bytes, (long long)ly.total);
   AFFB_REQUIRE(ly.total == 0 || workspace, "nbhd_attn_bwd: workspace is NULL");
+  if (tile_plan)
+    AFFB_REQUIRE(nbhd_tc_supported(dtype, D, M) && tile_plan_bytes >= nbhd_tile_plan_bytes(B, N, M) &&
+                     ((uintptr_t)tile_plan & 15) == 0,
+                 "nbhd_attn_bwd: the tile plan must come from the tensor-core forward of the same sizes");
   if (B == 0 || N == 0) return AFFB_OK;
   AFFB_REQUIRE(B * N * (M / 8) < (1ll << 31), "nbhd_attn_bwd: too many list entries");
   NbhdArgs a = make_args(q, k, v, member_idx, bias, mask, mask_heads, blank_k, blank_v, B, H, N, D, M, scale);
@@ -174,7 +205,9 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
     ag.dbv = nullptr;
     if (int e = nbhd_blk_bwd(ag, dtype, (int)B, st)) return e;
     if (int e = nbhd_kv_bwd(a, kv, dtype, (int)B, st)) return e;
-    if (int e = nbhd_blk_dq(a, dtype, (int)B, st)) return e;
+    NbhdArgs aq = a;
+    aq.tile_plan = const_cast<void*>(tile_plan);
+    if (int e = nbhd_blk_dq(aq, dtype, (int)B, st)) return e;
   } else {
     float* sk = dtype == AFFB_F32 ? (float*)dk : ly.acc_k;
     float* sv = dtype == AFFB_F32 ? (float*)dv : ly.acc_v;
@@ -195,4 +228,32 @@ extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, c
   }
   AFFB_LAUNCH_CHECK("affb_nbhd_attn_bwd");
   return AFFB_OK;
+}
+
+extern "C" int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                                  const void* dout, const float* lse,
+                                  const int32_t* member_idx, const void* bias,
+                                  const uint8_t* mask, int mask_heads, const void* blank_k,
+                                  const void* blank_v, int dtype, int64_t B, int64_t H,
+                                  int64_t N, int64_t D, int64_t M, float scale, void* dq,
+                                  void* dk, void* dv, void* dbias, float* dbk_acc,
+                                  float* dbv_acc, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+  return nbhd_bwd_impl(q, k, v, o, dout, lse, member_idx, bias, mask, mask_heads, blank_k, blank_v, dtype, B, H, N,
+                       D, M, scale, dq, dk, dv, dbias, dbk_acc, dbv_acc, nullptr, 0, workspace, workspace_bytes,
+                       stream);
+}
+
+extern "C" int affb_nbhd_attn_bwd_plan(const void* q, const void* k, const void* v, const void* o,
+                                       const void* dout, const float* lse, const int32_t* member_idx,
+                                       const void* bias, const uint8_t* mask, int mask_heads, const void* blank_k,
+                                       const void* blank_v, int dtype, int64_t B, int64_t H, int64_t N, int64_t D,
+                                       int64_t M, float scale, void* dq, void* dk, void* dv, void* dbias,
+                                       float* dbk_acc, float* dbv_acc, const void* tile_plan,
+                                       int64_t tile_plan_bytes, void* workspace, int64_t workspace_bytes,
+                                       void* stream) {
+  AFFB_REQUIRE(tile_plan != nullptr, "nbhd_attn_bwd_plan: tile plan is NULL (use affb_nbhd_attn_bwd)");
+  return nbhd_bwd_impl(q, k, v, o, dout, lse, member_idx, bias, mask, mask_heads, blank_k, blank_v, dtype, B, H, N,
+                       D, M, scale, dq, dk, dv, dbias, dbk_acc, dbv_acc, tile_plan, tile_plan_bytes, workspace,
+                       workspace_bytes, stream);
 }

@@ -68,6 +68,49 @@ struct BlkWarpDq {
   alignas(16) T dS[TQ * MM + 8];
   alignas(16) T K[2][16 * TD];
 };
+// A tile's cluster union as the forward built it, kept for the dQ kernel of
+// the backward (same neighbour lists and mask): nclu (-1 for a tile that is
+// not of cluster-run form), the cluster ids and the run-offset table.
+template <int MM>
+struct TilePlan {
+  int nclu;
+  int pad[3];
+  int uclu[BlkSetup<MM>::UCL];
+  int16_t boff[TQ][BlkSetup<MM>::UCL];
+};
+
+template <int MM>
+__device__ __forceinline__ void tile_plan_store(TilePlan<MM>* tp, const BlkSetup<MM>& s, int nclu) {
+  const int t = threadIdx.x;
+  if (t == 0) tp->nclu = nclu;
+  if (nclu <= 0) return;
+  for (int i = t; i < nclu; i += TC_THREADS) tp->uclu[i] = s.uclu[i];
+  for (int i = t; i < TQ * nclu; i += TC_THREADS) {
+    const int r = i / nclu, u = i - r * nclu;
+    tp->boff[r][u] = s.boff[r][u];
+  }
+}
+
+// Returns the tile's nclu; its tables are in s after the block barrier.  The
+// chunk loops read cluster slots in pairs, so with an odd count the slot
+// after the last one is set to the absent-cluster offset, as blk_setup
+// leaves it.
+template <int MM>
+__device__ __forceinline__ int tile_plan_load(const TilePlan<MM>* tp, BlkSetup<MM>& s) {
+  const int t = threadIdx.x;
+  const int nclu = tp->nclu;
+  if (nclu > 0) {
+    const int ncol = min(nclu + (nclu & 1), BlkSetup<MM>::UCL);
+    for (int i = t; i < nclu; i += TC_THREADS) s.uclu[i] = tp->uclu[i];
+    for (int i = t; i < TQ * ncol; i += TC_THREADS) {
+      const int r = i / ncol, u = i - r * ncol;
+      s.boff[r][u] = u < nclu ? tp->boff[r][u] : (int16_t)(TQ * MM);
+    }
+  }
+  __syncthreads();
+  return nclu;
+}
+
 // The staged neighbour rows are read only by the setup, before any warp
 // buffer is written, so they share storage with the warps' buffers.
 template <int MM, typename W>
@@ -375,6 +418,7 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_FWD_MINB) nbhd_blk_fwd_kernel
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
   const int nclu = blk_setup<MM>(s.setup, s.u.idx, a, b, n0, nq);
+  if (a.tile_plan) tile_plan_store<MM>(reinterpret_cast<TilePlan<MM>*>(a.tile_plan) + blockIdx.x, s.setup, nclu);
   const int warp = threadIdx.x >> 5;
   if (nclu < 0) {  // not cluster-block lists: CUDA-core rows
     for (int w = warp; w < a.H * nq; w += NW) nbhd_fwd_row<T, 4>(a, b, w / nq, n0 + w % nq);
@@ -611,7 +655,9 @@ __global__ void __launch_bounds__(TC_THREADS, AFFB_DQ_MINB) nbhd_blk_dq_kernel(N
   const int b = blockIdx.x / tiles;
   const int n0 = (blockIdx.x % tiles) * TQ;
   const int nq = min(TQ, N - n0);
-  const int nclu = blk_setup<MM>(s.setup, s.u.idx, a, b, n0, nq);
+  const int nclu = a.tile_plan ? tile_plan_load<MM>(reinterpret_cast<const TilePlan<MM>*>(a.tile_plan) + blockIdx.x,
+                                                   s.setup)
+                               : blk_setup<MM>(s.setup, s.u.idx, a, b, n0, nq);
   if (nclu < 0) return;  // excluded by the list check that cleared the flag
   const int warp = threadIdx.x >> 5;
   for (int h = warp; h < a.H; h += NW) blk_dq_head<T, MM>(a, s.setup, s.u.w[warp], b, h, n0, nq, nclu);
@@ -647,6 +693,16 @@ static int blk_mm(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 6
                                          : launch_blk(KERNEL<__half, 64>, sizeof(SMEM<__half, 64>), a, B, st, MAXB);             \
     }                                                                                                     \
   } while (0)
+
+int64_t nbhd_tile_plan_bytes(int64_t B, int64_t N, int64_t M) {
+  const int64_t tiles = B * ((N + TQ - 1) / TQ);
+  switch (blk_mm((int)M)) {
+    case 16: return tiles * (int64_t)sizeof(TilePlan<16>);
+    case 32: return tiles * (int64_t)sizeof(TilePlan<32>);
+    case 48: return tiles * (int64_t)sizeof(TilePlan<48>);
+    default: return tiles * (int64_t)sizeof(TilePlan<64>);
+  }
+}
 
 int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) { AFFB_BLK_LAUNCH(nbhd_blk_fwd_kernel, BlkFwdSmem, 0); }
 int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st) {

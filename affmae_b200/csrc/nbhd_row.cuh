@@ -74,6 +74,9 @@ struct NbhdArgs {
   // does the whole backward, scatter-adding dK / dV into dk / dv), dS in bias
   // layout [B,H,N,M] and the blank token's dS per (b, h, n)
   const int* general;
+  // optional per-tile cluster unions (nbhd_attn_blk.cu TilePlan): written by
+  // the forward, read by the dQ kernel instead of rebuilding them
+  void* tile_plan;
   const void* ds;
   const float* dsb;
 };

@@ -81,7 +81,10 @@ struct KvArgs {
   int Cc;  // key clusters per image, ceil(N / 8)
 };
 
-// Query side (nbhd_attn_blk.cu).
+// Query side (nbhd_attn_blk.cu).  A forward given a.tile_plan (of
+// nbhd_tile_plan_bytes) stores its tiles' cluster unions there; a backward
+// given the same plan skips rebuilding them in the dQ kernel.
+int64_t nbhd_tile_plan_bytes(int64_t B, int64_t N, int64_t M);
 int nbhd_blk_fwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 int nbhd_blk_bwd(const NbhdArgs& a, int dtype, int B, cudaStream_t st);
 int nbhd_blk_dq(const NbhdArgs& a, int dtype, int B, cudaStream_t st);

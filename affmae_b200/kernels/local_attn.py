@@ -35,8 +35,12 @@ def _prep_mask(mask, B, H, N, M):
 
 
 def launch_flash_nbhood_attn_fwd(q, k, v, member_index, sm_scale, bias=None, mask=None,
-                                 blank_k=None, blank_v=None, exp2=False):
-    """Forward: returns (o [B,H,N,D] in q.dtype, lse [B,H,N] fp32)."""
+                                 blank_k=None, blank_v=None, exp2=False, return_plan=False):
+    """Forward: returns (o [B,H,N,D] in q.dtype, lse [B,H,N] fp32).
+
+    ``return_plan=True`` also returns the tiles' cluster unions the forward
+    built (a byte tensor, or None off the tensor-core path), which
+    ``launch_flash_nbhood_attn_bwd(..., plan=...)`` reuses for the same lists."""
     assert q.shape == k.shape and k.shape == v.shape, "q, k, v must have the same shape"
     assert q.dim() == 4, "q, k, v must have 4 dimensions"
     assert q.shape[-1] % 8 == 0, "head_dim must be a multiple of 8"
@@ -64,15 +68,27 @@ def launch_flash_nbhood_attn_fwd(q, k, v, member_index, sm_scale, bias=None, mas
     m8, mh = _prep_mask(mask, B, H, N, M)
     o = torch.empty_like(q)
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    nat.call("affb_nbhd_attn_fwd", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(mi), nat.ptr(bias),
-             nat.ptr(m8), mh, nat.ptr(blank_k), nat.ptr(blank_v), nat.dcode(q), B, H, N, D, M,
-             float(sm_scale), nat.ptr(o), nat.ptr(lse), nat.stream(q.device))
+    plan = None
+    if return_plan:
+        pb = int(nat.lib().affb_nbhd_tile_plan_bytes(nat.dcode(q), B, N, D, M))
+        plan = torch.empty((pb,), device=q.device, dtype=torch.uint8) if pb > 0 else None
+    if plan is not None:
+        nat.call("affb_nbhd_attn_fwd_plan", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(mi), nat.ptr(bias),
+                 nat.ptr(m8), mh, nat.ptr(blank_k), nat.ptr(blank_v), nat.dcode(q), B, H, N, D, M,
+                 float(sm_scale), nat.ptr(o), nat.ptr(lse), nat.ptr(plan), plan.numel(), nat.stream(q.device))
+    else:
+        nat.call("affb_nbhd_attn_fwd", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(mi), nat.ptr(bias),
+                 nat.ptr(m8), mh, nat.ptr(blank_k), nat.ptr(blank_v), nat.dcode(q), B, H, N, D, M,
+                 float(sm_scale), nat.ptr(o), nat.ptr(lse), nat.stream(q.device))
+    if return_plan:
+        return o, lse, plan
     return o, lse
 
 
 def launch_flash_nbhood_attn_bwd(q, k, v, member_index, sm_scale, o, lse, do, bias=None,
-                                 mask=None, blank_k=None, blank_v=None, exp2=False):
-    """Backward: returns (dq, dk, dv, dbias | None, dblank_k | None, dblank_v | None)."""
+                                 mask=None, blank_k=None, blank_v=None, exp2=False, plan=None):
+    """Backward: returns (dq, dk, dv, dbias | None, dblank_k | None, dblank_v | None).
+    ``plan``: the forward's tile plan for the same lists and mask (optional)."""
     assert not exp2, "EXP2 is not supported in backward pass"
     assert q.shape == k.shape == v.shape == o.shape == do.shape
     assert q.dim() == 4
@@ -108,12 +124,15 @@ def launch_flash_nbhood_attn_bwd(q, k, v, member_index, sm_scale, o, lse, do, bi
     dbv = torch.zeros((H, D), device=dev, dtype=torch.float32) if has_blank else None
     wsb = int(nat.lib().affb_nbhd_attn_bwd_workspace_bytes(nat.dcode(q), B, H, N, D, M))
     ws = torch.empty((max(wsb, 1),), device=dev, dtype=torch.uint8)
-    nat.call("affb_nbhd_attn_bwd", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(o), nat.ptr(do),
-             nat.ptr(lse), nat.ptr(mi), nat.ptr(bias), nat.ptr(m8), mh,
-             nat.ptr(blank_k) if has_blank else None, nat.ptr(blank_v) if has_blank else None,
-             nat.dcode(q), B, H, N, D, M, float(sm_scale), nat.ptr(dq), nat.ptr(dk),
-             nat.ptr(dv), nat.ptr(dbias), nat.ptr(dbk), nat.ptr(dbv), nat.ptr(ws), wsb,
-             nat.stream(dev))
+    common = [nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(o), nat.ptr(do),
+              nat.ptr(lse), nat.ptr(mi), nat.ptr(bias), nat.ptr(m8), mh,
+              nat.ptr(blank_k) if has_blank else None, nat.ptr(blank_v) if has_blank else None,
+              nat.dcode(q), B, H, N, D, M, float(sm_scale), nat.ptr(dq), nat.ptr(dk),
+              nat.ptr(dv), nat.ptr(dbias), nat.ptr(dbk), nat.ptr(dbv)]
+    if plan is not None:
+        nat.call("affb_nbhd_attn_bwd_plan", *common, nat.ptr(plan), plan.numel(), nat.ptr(ws), wsb, nat.stream(dev))
+    else:
+        nat.call("affb_nbhd_attn_bwd", *common, nat.ptr(ws), wsb, nat.stream(dev))
     if has_blank:
         dbk = dbk.to(dt)
         dbv = dbv.to(dt)
@@ -135,13 +154,13 @@ class FlashLocalAttentionFunction(Function):
         has_blank = blank_k is not None and blank_v is not None
         has_mask = mask is not None and mask.numel() > 0
         member_idx = member_idx.to(torch.int32).contiguous()
-        out, lse = launch_flash_nbhood_attn_fwd(
+        out, lse, plan = launch_flash_nbhood_attn_fwd(
             Q, K, V, member_idx, softmax_scale, bias=bias if has_bias else None,
             mask=mask if has_mask else None, blank_k=blank_k if has_blank else None,
-            blank_v=blank_v if has_blank else None)
+            blank_v=blank_v if has_blank else None, return_plan=True)
         ctx.save_for_backward(Q, K, V, member_idx, bias if has_bias else None,
                               mask if has_mask else None, blank_k if has_blank else None,
-                              blank_v if has_blank else None, out, lse)
+                              blank_v if has_blank else None, out, lse, plan)
         ctx.scale = softmax_scale
         ctx.flags = (has_bias, has_blank, has_mask)
         return out
@@ -149,12 +168,12 @@ class FlashLocalAttentionFunction(Function):
     @staticmethod
     @custom_bwd(device_type="cuda")
     def backward(ctx, grad_output):
-        Q, K, V, member_idx, bias, mask, blank_k, blank_v, out, lse = ctx.saved_tensors
+        Q, K, V, member_idx, bias, mask, blank_k, blank_v, out, lse, plan = ctx.saved_tensors
         has_bias, has_blank, has_mask = ctx.flags
         dq, dk, dv, dbias, dbk, dbv = launch_flash_nbhood_attn_bwd(
             Q, K, V, member_idx, ctx.scale, out, lse, grad_output,
             bias=bias if has_bias else None, mask=mask if has_mask else None,
-            blank_k=blank_k if has_blank else None, blank_v=blank_v if has_blank else None)
+            blank_k=blank_k if has_blank else None, blank_v=blank_v if has_blank else None, plan=plan)
         dq, dk, dv = dq.to(Q.dtype), dk.to(K.dtype), dv.to(V.dtype)
         if has_bias:
             dbias = dbias.to(bias.dtype)

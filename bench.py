@@ -231,10 +231,12 @@ def run_gpu(args, world, rank, local):
     stream = torch.cuda.current_stream(dev)
 
     def step(ev=None):
-        o, lse = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, bias=bias, blank_k=bk, blank_v=bv)
+        o, lse, plan = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, bias=bias, blank_k=bk, blank_v=bv,
+                                                    return_plan=True)
         if ev is not None:
             ev[0].record(stream)
-        g = launch_flash_nbhood_attn_bwd(q, k, v, mi, scale, o, lse, do, bias=bias, blank_k=bk, blank_v=bv)
+        g = launch_flash_nbhood_attn_bwd(q, k, v, mi, scale, o, lse, do, bias=bias, blank_k=bk, blank_v=bv,
+                                         plan=plan)
         if ev is not None:
             ev[1].record(stream)
         return o, g
@@ -261,7 +263,8 @@ def run_gpu(args, world, rank, local):
             times.append((e0, ef, e1))
         torch.cuda.synchronize()
         # kernel-only bwd timing (the dominant kernel): events around the C call
-        o, lse = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, bias=bias, blank_k=bk, blank_v=bv)
+        o, lse, plan = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, bias=bias, blank_k=bk, blank_v=bv,
+                                                    return_plan=True)
         dq = torch.empty_like(q)
         dk = torch.empty_like(q)
         dv = torch.empty_like(q)
@@ -277,11 +280,11 @@ def run_gpu(args, world, rank, local):
             a = torch.cuda.Event(enable_timing=True)
             c = torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            nat.call("affb_nbhd_attn_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
-                     lse.data_ptr(), mi.data_ptr(), bias.data_ptr(), None, 1, bk.data_ptr(), bv.data_ptr(),
-                     nat.BF16, B, H, N, D, CFG["nbhd"], float(scale), dq.data_ptr(), dk.data_ptr(),
-                     dv.data_ptr(), dbias.data_ptr(), dbk.data_ptr(), dbv.data_ptr(), ws.data_ptr(), wsb,
-                     stream.cuda_stream)
+            nat.call("affb_nbhd_attn_bwd_plan", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                     do.data_ptr(), lse.data_ptr(), mi.data_ptr(), bias.data_ptr(), None, 1, bk.data_ptr(),
+                     bv.data_ptr(), nat.BF16, B, H, N, D, CFG["nbhd"], float(scale), dq.data_ptr(),
+                     dk.data_ptr(), dv.data_ptr(), dbias.data_ptr(), dbk.data_ptr(), dbv.data_ptr(),
+                     plan.data_ptr(), plan.numel(), ws.data_ptr(), wsb, stream.cuda_stream)
             c.record(stream)
             kern_ms.append((a, c))
         torch.cuda.synchronize()
@@ -386,7 +389,7 @@ def run_gpu(args, world, rank, local):
                 "e2e": None if e2e_value is None else {
                     "value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_s * 1e3 / args.steps},
-                "roofline": {"kernel": "affb_nbhd_attn_bwd (list, query-side and key-side kernels)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                "roofline": {"kernel": "affb_nbhd_attn_bwd_plan (list, prologue, key-side and dQ kernels)", "bound": "hbm", "achieved": achieved, "peak": peak,
                              "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                              "traffic": BWD_DRAM_BYTES_PER_IMAGE * CFG["B"],
                              "traffic_note": "ncu dram__bytes_read+write of the backward kernels at B=16, scaled by B",

@@ -101,6 +101,29 @@ int affb_nbhd_attn_bwd(const void* q, const void* k, const void* v, const void* 
                        void* dk, void* dv, void* dbias, float* dbk_acc, float* dbv_acc,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The same forward and backward sharing the tiles' cluster unions (no
+ * counterpart in the reference, whose backward re-reads member_idx per query
+ * block).  On the tensor-core path (bf16 / fp16, D == 32, M <= 64) the
+ * forward builds, per tile of 16 queries, the union of the key clusters they
+ * list and a run-offset table; affb_nbhd_attn_fwd_plan also stores them in
+ * `tile_plan` (affb_nbhd_tile_plan_bytes(...) bytes, 16-byte aligned; 0
+ * bytes off the tensor-core path), and affb_nbhd_attn_bwd_plan's dQ kernel
+ * reads them instead of rebuilding them.  The plan is valid for the
+ * member_idx and mask of the forward that wrote it.                        */
+int64_t affb_nbhd_tile_plan_bytes(int dtype, int64_t B, int64_t N, int64_t D, int64_t M);
+int affb_nbhd_attn_fwd_plan(const void* q, const void* k, const void* v, const int32_t* member_idx,
+                            const void* bias, const uint8_t* mask, int mask_heads, const void* blank_k,
+                            const void* blank_v, int dtype, int64_t B, int64_t H, int64_t N, int64_t D,
+                            int64_t M, float scale, void* out, float* lse, void* tile_plan,
+                            int64_t tile_plan_bytes, void* stream);
+int affb_nbhd_attn_bwd_plan(const void* q, const void* k, const void* v, const void* o,
+                            const void* dout, const float* lse, const int32_t* member_idx,
+                            const void* bias, const uint8_t* mask, int mask_heads, const void* blank_k,
+                            const void* blank_v, int dtype, int64_t B, int64_t H, int64_t N, int64_t D,
+                            int64_t M, float scale, void* dq, void* dk, void* dv, void* dbias,
+                            float* dbk_acc, float* dbv_acc, const void* tile_plan, int64_t tile_plan_bytes,
+                            void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ relative-position bias --
  * Replaces the gather of ClusterAttention._make_pos_bias
  * (src/layers/attention.py:110-124):

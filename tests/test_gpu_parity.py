@@ -714,3 +714,40 @@ def test_reference_public_helpers(cuda):
     assert torch.allclose(sw.sum(-1), torch.ones_like(sw.sum(-1)))
     fd.set_use_heuristics(False)
     fd.set_use_heuristics(True)
+
+
+@pytest.mark.parametrize("variant", ["clusters", "ragged_masked", "general"])
+def test_local_attn_tile_plan_reuse(cuda, variant):
+    """The backward given the forward's tile plan (its tiles' cluster unions)
+    returns exactly the gradients of the backward that rebuilds them."""
+    from affmae_b200.kernels.local_attn import launch_flash_nbhood_attn_fwd, launch_flash_nbhood_attn_bwd
+    from affmae_b200.mae import curve_clusters, neighbourhood
+    from affmae_b200.workloads import nbhd_attention_inputs
+    if variant == "clusters":
+        inp = nbhd_attention_inputs(B=2, side=48, H=4, dtype=torch.bfloat16, seed=6, device=cuda)
+        q, k, v, mi, do = inp["q"], inp["k"], inp["v"], inp["member_idx"], inp["dout"]
+        kw = dict(bias=inp["bias"], blank_k=inp["blank_k"], blank_v=inp["blank_v"])
+        scale = inp["scale"]
+    else:
+        g = golden("clusters_ragged")
+        pos, means, cmask, _ = curve_clusters(g["pos"].to(cuda), 8, 64, 64)
+        member, mask, _ = neighbourhood(pos, means, cmask, 48, 8)
+        B, N, M = member.shape
+        d = _attn_inputs(B, 2, N, 32, M, torch.float16, mask=False, seed=22)
+        m = mask.clone()
+        if variant == "general":
+            m[tuple((~m).nonzero()[0])] = True
+        G = _to(d, cuda)
+        q, k, v, mi, do = G["q"], G["k"], G["v"], member.to(torch.int32), G["do"]
+        kw = dict(bias=G["bias"], mask=m[:, None], blank_k=G["blank_k"], blank_v=G["blank_v"])
+        scale = 32 ** -0.5
+    o, lse, plan = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, return_plan=True, **kw)
+    o2, lse2 = launch_flash_nbhood_attn_fwd(q, k, v, mi, scale, **kw)
+    assert plan is not None and torch.equal(o, o2) and torch.equal(lse, lse2)
+    g1 = launch_flash_nbhood_attn_bwd(q, k, v, mi, scale, o, lse, do, plan=plan, **kw)
+    g2 = launch_flash_nbhood_attn_bwd(q, k, v, mi, scale, o, lse, do, **kw)
+    for name, a, b in zip(["dq", "dk", "dv", "dbias"], g1[:4], g2[:4]):
+        if variant == "general" and name in ("dk", "dv"):  # scatter-added: order of the adds is free
+            assert rel_err(a.float().cpu(), b.float().cpu()) < 1e-2, name
+        else:
+            assert torch.equal(a, b), name

@@ -429,9 +429,13 @@ __device__ __forceinline__ void kv_segment(const NbhdArgs& a, const KvHead<T>& p
       const float p1 = v1 ? __expf(sc[2 * hf + 1] * a.scale + b1 - ls) : 0.f;
       pp[hf] = pack2<T>(p0, p1);
       pd[hf] = pack2<T>(p0 * (dp[2 * hf] - dd), p1 * (dp[2 * hf + 1] - dd));
-      // dS in bias layout: run j of query q, columns 2tq, 2tq+1
-      if (row < nr) *reinterpret_cast<uint32_t*>(p.ds + s.roff[ch * 16 + row] + 2 * tq) = pd[hf];
+      // dS of the chunk staged as 16 runs of 8 (16 bytes each) for one vector store per run
+      reinterpret_cast<uint32_t*>(w.ost)[row * 4 + tq] = pd[hf];
     }
+    __syncwarp();
+    // dS in bias layout: the run of query q's list position j (16-byte aligned: offset q*M + 8j)
+    if (lane < 16 && lane < nr)
+      *reinterpret_cast<uint4*>(p.ds + s.roff[ch * 16 + lane]) = reinterpret_cast<const uint4*>(w.ost)[lane];
     const uint32_t bp[2] = {movmatrix_t(pp[0]), movmatrix_t(pp[1])};
     const uint32_t bd[2] = {movmatrix_t(pd[0]), movmatrix_t(pd[1])};
     const int mi = lane >> 3;

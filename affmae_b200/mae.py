@@ -209,12 +209,21 @@ class ClusterAttention(nn.Module):
         self.pos_embed = Linear(5, heads)
         self.proj = Linear(dim, dim)
 
-    def forward(self, feat, member_idx, mask, pe_idx):
+    def forward(self, feat, member_idx, mask, pe_idx, global_attn: bool = False):
         B, N, C = feat.shape
         H, d = self.heads, C // self.heads
         q = split_heads(self.q(feat), H)
         k, v = split_heads(self.kv(feat), H, 2)
         bias = rel_pos_bias(self.pos_embed.weight, self.pos_embed.bias, pe_idx, q.dtype)  # [B,H,N,M]
+        if global_attn:
+            # every token attends every token plus the blank token
+            # (attention.py:157-180): pe_idx is [B,N,N]; the bias gets a zero
+            # column for the blank key; PyTorch's fused attention (library code)
+            bias = F.pad(bias, (0, 1))
+            bk = self.blank_k.view(1, H, 1, d).expand(B, -1, -1, -1).to(q.dtype)
+            bv = self.blank_v.view(1, H, 1, d).expand(B, -1, -1, -1).to(q.dtype)
+            out = F.scaled_dot_product_attention(q, torch.cat([k, bk], 2), torch.cat([v, bv], 2), attn_mask=bias)
+            return self.proj(merge_heads(out.contiguous()))
         out = FlashLocalAttentionFunction.apply(
             q, k, v, member_idx, bias, None if mask is None else mask[:, None],
             self.blank_k.view(H, d), self.blank_v.view(H, d), float(self.scale))
@@ -232,10 +241,10 @@ class ClusterBlock(nn.Module):
         self.fc2 = Linear(hidden, dim)
         self.drop_path = DropPath(drop_path)
 
-    def forward(self, feat, member_idx, mask, pe_idx):
+    def forward(self, feat, member_idx, mask, pe_idx, global_attn: bool = False):
         # pre-norms feed only Linears: produced directly in the autocast dtype
         h = self.norm1(feat, out32=False, out16=True)
-        feat = feat + self.drop_path(self.attn(h, member_idx, mask, pe_idx))
+        feat = feat + self.drop_path(self.attn(h, member_idx, mask, pe_idx, global_attn))
         h = self.norm2(feat, out32=False, out16=True)
         return feat + self.drop_path(self.fc2(F.gelu(self.fc1(h))))
 
@@ -292,8 +301,13 @@ class Stage(nn.Module):
         pos, means, cmask, order = curve_clusters(pos, m, h, w)
         feat = feat.gather(1, order[..., None].expand(-1, -1, C))
         member, mask, pe_idx = neighbourhood(pos, means, cmask, self.cfg.nbhd_size, m)
+        global_attn = self.cfg.nbhd_size >= n  # BasicLayer.forward, aff.py:421-424
+        att_pe = pe_idx
+        if global_attn:  # relative indices of every token pair (aff.py:458-459)
+            rel = ((pos[:, None, :, :] + REL_POS_WIDTH) - pos[:, :, None, :]).clamp(0, TABLE_WIDTH - 1)
+            att_pe = (rel[..., 1] * TABLE_WIDTH + rel[..., 0]).long()
         for blk in self.blocks:
-            feat = blk(feat, member, mask, pe_idx)
+            feat = blk(feat, member, mask, att_pe, global_attn)
         if self.merge is None:
             return pos, feat, pos, feat
         importance = self.prob_net(feat).sigmoid()

@@ -242,6 +242,40 @@ def gen_decoder_block(root):
          dout=dout, d_query=query.grad, d_src=src.grad, dim=64, heads=2, ffn=128)
 
 
+def gen_global(A):
+    """The global path of a stage with no more tokens than the neighbourhood
+    size (aff.py:421-424, attention.py:157-180): ClusterAttention over all
+    token pairs plus the blank token, and BasicLayer (one block, no merging)
+    on 40 tokens in a 16x16 canvas."""
+    import importlib
+    aff = importlib.import_module("src.layers.aff")
+    g = torch.Generator().manual_seed(17)
+    m = A.ClusterAttention(64, 2)
+    randomise(m, g)
+    N = 40
+    pos = torch.rand((1, N, 2), generator=g) * 16
+    rel = ((pos[:, None, :, :] + 127) - pos[:, :, None, :]).clamp(0, 254)
+    pe_idx = (rel[..., 1] * 255 + rel[..., 0]).long()
+    feat = torch.randn((1, N, 64), generator=g).requires_grad_(True)
+    dout = torch.randn((1, N, 64), generator=g)
+    out = m(feat, torch.zeros((1, N, N), dtype=torch.long), None, pe_idx, True)  # the list is not read
+    out.backward(dout)
+    save("cluster_attention_global", m, feat=feat, pe_idx=pe_idx, dout=dout, out=out, d_feat=feat.grad, dim=64,
+         heads=2)
+    st = aff.BasicLayer(64, None, cluster_size=8, nbhd_size=48, depth=1, num_heads=2, mlp_ratio=2.0)
+    randomise(st, g)
+    with torch.no_grad():
+        for mod in st.modules():
+            if isinstance(mod, torch.nn.LayerNorm):
+                mod.weight.add_(1.0)
+    feat = torch.randn((1, N, 64), generator=g).requires_grad_(True)
+    pos_o, feat_o, _, _ = st(pos, feat, 16, 16, False, 2)
+    d_o = torch.randn(feat_o.shape, generator=g)
+    feat_o.backward(d_o)
+    save("stage_global", st, pos=pos, feat=feat, pos_out=pos_o, feat_out=feat_o, d_out=d_o, d_feat=feat.grad,
+         dim=64, heads=2, depth=1, hw=16)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
@@ -257,6 +291,7 @@ def main():
     gen_cluster_merging(A, a.reference)
     gen_stage(A, a.reference)
     gen_decoder_block(a.reference)
+    gen_global(A)
 
 
 if __name__ == "__main__":

@@ -36,3 +36,42 @@ def test_patch_reference_rebinds_kernel_and_layer_names():
     finally:
         for n in names:
             sys.modules.pop(n, None)
+
+
+def test_patch_reference_on_the_real_reference_tree():
+    """patch_reference() on the reference's own modules (imported from the
+    checkout named by AFFMAE_REFERENCE, with the same stubs as the fixture
+    generators: the GPU-driver query of kernels/util.py and the unused
+    pykeops / timm / fvcore imports): every operator name the layer modules
+    use is rebound to this package, and the modules' classes are untouched."""
+    import os
+    import pytest
+    root = os.environ.get("AFFMAE_REFERENCE")
+    if not root:
+        pytest.skip("AFFMAE_REFERENCE (a checkout of the reference) is not set")
+    sys.path.insert(0, str(__import__("pathlib").Path(__file__).resolve().parent / "golden"))
+    saved = {k: v for k, v in sys.modules.items() if k == "src" or k.startswith("src.")}
+    try:
+        from make_module_golden import load_attention
+        import importlib
+        load_attention(root)
+        att = importlib.import_module("src.layers.attention")
+        aff = importlib.import_module("src.layers.aff")
+        done = patch.patch_reference("src")
+        from affmae_b200.kernels import fused_deform_attn, msdetrpc
+        assert att.FlashLocalAttentionFunction is local_attn.FlashLocalAttentionFunction
+        assert att.launch_flash_nbhood_attn_fwd is local_attn.launch_flash_nbhood_attn_fwd
+        assert att.fused_knn_deformable_cross_attention is fused_deform_attn.fused_knn_deformable_cross_attention
+        assert att.fused_knn_deformable_self_attention is fused_deform_attn.fused_knn_deformable_self_attention
+        assert att.fused_deformable_attention is fused_deform_attn.fused_deformable_attention
+        assert att.MSDETRPCFunction is msdetrpc.MSDETRPCFunction
+        assert att.triton_knn is knn.knn
+        assert aff.triton_knn is knn.knn and aff.weighted_features is weighted_features.weighted_features
+        kmod = importlib.import_module("src.layers.kernels.local_attn")
+        assert kmod.FlashLocalAttentionFunction is local_attn.FlashLocalAttentionFunction
+        assert att.ClusterAttention.__module__ == "src.layers.attention"
+        assert len(done) >= 10
+    finally:
+        for k in [k for k in sys.modules if k == "src" or k.startswith("src.")]:
+            del sys.modules[k]
+        sys.modules.update(saved)

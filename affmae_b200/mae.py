@@ -86,6 +86,35 @@ def curve_clusters(pos: torch.Tensor, m: int, h: int, w: int):
     cluster_mask [B,k,m] long or None when n % m == 0, order [B,n] with
     order[b, i] = original index of the i-th token).
     """
+    return clusters_in_order(pos, curve_key(pos, m, h, w).argsort(dim=1), m)
+
+
+def clusters_in_order(pos: torch.Tensor, order: torch.Tensor, m: int):
+    """The outputs of curve_clusters for a given token order [B,n]: runs of m
+    tokens along it are the clusters, the last one partial when m does not
+    divide n."""
+    pos = pos.detach().float()
+    B, n, _ = pos.shape
+    dev = pos.device
+    k = math.ceil(n / m)
+    pos = pos.gather(1, order[..., None].expand(-1, -1, 2))
+    if k * m == n:
+        return pos, pos.view(B, k, m, 2).mean(2), None, order
+    padded = torch.zeros((B, k * m, 2), device=dev)
+    padded[:, :n] = pos
+    cmask = torch.zeros((B, k * m), device=dev, dtype=torch.long)
+    cmask[:, :n] = 1
+    cmask = cmask.view(B, k, m)
+    means = padded.view(B, k, m, 2).sum(2) / cmask.sum(2, keepdim=True)
+    return pos, means, cmask, order
+
+
+@torch.no_grad()
+def curve_key(pos: torch.Tensor, m: int, h: int, w: int) -> torch.Tensor:
+    """The scan rank of every token [B,n] fp32 (cell visiting order scaled
+    above the largest within-cell distance ratio, plus the ratio): sorting
+    it gives the cluster order.  Tokens with equal keys are left in the
+    order the sort implementation picks, as in the reference."""
     pos = pos.detach().float()
     B, n, _ = pos.shape
     dev = pos.device
@@ -108,18 +137,7 @@ def curve_clusters(pos: torch.Tensor, m: int, h: int, w: int):
     d_prev = (pos - prev[rank]).pow(2).sum(-1)
     d_next = (pos - nxt[rank]).pow(2).sum(-1)
     ratio = d_prev / (d_next + 1e-5)
-    key = rank.float() * (ratio.max() + 1) + ratio
-    order = key.argsort(dim=1)
-    pos = pos.gather(1, order[..., None].expand(-1, -1, 2))
-    if k * m == n:
-        return pos, pos.view(B, k, m, 2).mean(2), None, order
-    padded = torch.zeros((B, k * m, 2), device=dev)
-    padded[:, :n] = pos
-    cmask = torch.zeros((B, k * m), device=dev, dtype=torch.long)
-    cmask[:, :n] = 1
-    cmask = cmask.view(B, k, m)
-    means = padded.view(B, k, m, 2).sum(2) / cmask.sum(2, keepdim=True)
-    return pos, means, cmask, order
+    return rank.float() * (ratio.max() + 1) + ratio
 
 
 def neighbourhood(pos: torch.Tensor, means: torch.Tensor, cmask, nbhd: int, m: int):

@@ -247,7 +247,20 @@ OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_defo
        "deform-mae-raster": lambda: op_deform_mae(raster=True), "wfeat": op_wfeat,
        "wfeat-fwd": lambda: op_wfeat(fwd_only=True),
        "wgather": op_wgather, "layer-norm": op_layer_norm, "rel-bias": op_rel_bias,
-       "head-layout": op_head_layout, "deform-nbidx": op_deform_nbidx}
+       "head-layout": op_head_layout, "deform-nbidx": op_deform_nbidx, "tile-union": None}
+
+
+def op_tile_union():
+    """Config 3 lists (curve order): distinct key clusters per tile of T
+    consecutive queries, i.e. the pairs a query-tiled kernel computes against
+    the 48 listed per query, for the tile heights of mma.sync (16) and of
+    tcgen05 (64 / 128 rows).  Host only."""
+    from .workloads import clustered_tokens, neighbourhoods, tile_union
+    member, _ = neighbourhoods(clustered_tokens(4, 96, 0.5, 0, "cpu"), 8, 48)
+    for t in (8, 16, 32, 64, 128):
+        u = tile_union(member, t)
+        print(json.dumps({"op": "tile-union", "tile_queries": t, "clusters": round(u, 2), "keys": round(8 * u, 1),
+                          "computed_per_listed": round(8 * u / 48, 2)}), flush=True)
 
 
 def main():
@@ -255,6 +268,9 @@ def main():
     ap.add_argument("op", choices=sorted(OPS))
     ap.add_argument("--iters", type=int, default=20)
     a = ap.parse_args()
+    if a.op == "tile-union":
+        op_tile_union()
+        return
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     fn, nbytes, cfg = OPS[a.op]()
     ms = _time(fn, a.iters, flush)

@@ -127,6 +127,19 @@ def nbhd_attention_inputs(B=32, side=96, keep=0.5, H=4, d=32, nbhd=48, dtype=tor
                 blank_v=rnd(H, d, std=0.2), dout=rnd(B, H, N, d), scale=s, pos=pos)
 
 
+def tile_union(member_idx: torch.Tensor, tile: int, cluster: int = 8) -> float:
+    """Mean number of distinct key clusters listed by a tile of ``tile``
+    consecutive queries (lists of whole clusters, [B,N,M]): the keys a
+    query-tiled kernel computes per tile are cluster x this, against M listed
+    per query."""
+    B, N, M = member_idx.shape
+    clu = (member_idx[..., ::cluster] // cluster).long()
+    n = (N // tile) * tile
+    c = clu[:, :n].reshape(B * (n // tile), tile * (M // cluster))
+    s = c.sort(dim=1).values
+    distinct = 1 + (s[:, 1:] != s[:, :-1]).sum(1)
+    return distinct.double().mean().item()
+
 def nbhd_attention_bytes(B, H, N, d, M, elem=2):
     """Algorithmic (interface) bytes of one forward and one backward call."""
     T = B * H * N * d * elem

@@ -276,15 +276,147 @@ def gen_global(A):
          dim=64, heads=2, depth=1, hw=16)
 
 
+MODEL_CFG = dict(img_size=100, patch_size=4, mask_ratio=0.488, embed_dims=(32, 32, 64, 64),
+                 depths=(2, 1, 1, 1), num_heads=(1, 1, 2, 2), decoder_dim=64, decoder_heads=2)
+
+
+def bind_cpu_wrappers(aff):
+    """Bind the two CUDA-asserting wrappers the encoder calls for a CPU run:
+    ``weighted_features`` (weighted_features.py:411) to the reference's own
+    launchers one layer down, ``knn`` (knn.py:1384) to the oracle's exact KNN
+    (the reference kernel's (distance, index) order, pinned by the KNN golden
+    vectors)."""
+    import importlib
+    sys.path.insert(0, str(HERE.parent.parent))
+    import oracle
+    wf = importlib.import_module("src.layers.kernels.weighted_features")
+
+    class WF(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, w, f, idx):
+            ctx.save_for_backward(w, f, idx)
+            return wf.weighted_features_triton(w, f, idx.to(torch.int32))
+
+        @staticmethod
+        def backward(ctx, dout):
+            w, f, idx = ctx.saved_tensors
+            dw, df = wf.weighted_features_triton_backward(dout.contiguous(), w, f, idx.to(torch.int32))
+            return dw, df, None
+
+    aff.weighted_features = WF.apply
+    aff.triton_knn = lambda q, r, k, **kw: oracle.knn(q, r, k)
+
+
+def gen_model(root, seeds=range(40, 60)):
+    """The whole masked autoencoder, AFFMaskedAutoEncoder (aff_mae.py:26-205)
+    with cluster merging, at a reduced size: one 100 x 100 image, patch 4, a
+    25 x 25 token canvas with 320 visible tokens -> 128 -> 51 -> 20 (stages 1-3
+    attend locally, the last one partially filled clusters, stage 4 globally)
+    and 305 masked-patch queries; decoder width 64; the reference's own
+    initialisation; eval mode (no dropout); fp32; loss and every parameter
+    gradient.  The sizes keep the reference's decoder, whose deformable kernels
+    scan every key per sample, to minutes under the interpreter.
+
+    The token mask is an input: the reference draws it from Perlin noise (an
+    absent package), so its masking call is given the split of a stored noise
+    tensor, with the masked ids in raster order (the order this package's
+    decoder uses; the loss does not depend on it).
+
+    Two decision boundaries are pinned so that the comparison does not sit
+    on one.  (1) The clustering sorts a key in which grid positions tie (the
+    perpendicular bisector of two anchors, mirror images across an anchor
+    row) and the order of tied tokens is left to the sort implementation: the
+    order the reference chose at every stage is stored (``stage{i}.pos``, the
+    positions in cluster order) for the comparison to follow within tied
+    runs.  (2) A seed is kept only if each merging's importance top-k has a
+    gap above 2e-3 between the last kept and the first dropped score (the
+    reference rounds attention outputs through fp16, which moves the scores
+    by about 1e-4); that is checked on the encoder alone before the full
+    run."""
+    import importlib
+    for name in ("perlin_noise", "cv2", "matplotlib", "matplotlib.pyplot"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["perlin_noise"].perlin_noise = None
+    sys.modules["matplotlib"].pyplot = sys.modules["matplotlib.pyplot"]
+    m = types.ModuleType("src.models")
+    m.__path__ = [f"{root}/src/models"]
+    sys.modules["src.models"] = m
+    aff = importlib.import_module("src.layers.aff")
+    mae_ref = importlib.import_module("src.models.aff_mae")
+    bind_cpu_wrappers(aff)
+    rec = {"pos": [], "gaps": []}
+    cluster = aff.space_filling_cluster
+
+    def recorded_cluster(pos, *a, **kw):
+        out = cluster(pos, *a, **kw)
+        rec["pos"].append(out[0].detach().clone())
+        return out
+
+    aff.space_filling_cluster = recorded_cluster
+    merge_fwd = aff.ClusterMerging.forward
+
+    def checked_merge(self, pos, feat, member_idx, cluster_mask, learned_prob, *a, **kw):
+        lp = learned_prob.detach().view(feat.shape[0], -1).sort(dim=1, descending=True).values
+        keep = int(feat.shape[1] * self.ds_rate)
+        rec["gaps"].append((lp[:, keep - 1] - lp[:, keep]).min().item())
+        return merge_fwd(self, pos, feat, member_idx, cluster_mask, learned_prob, *a, **kw)
+
+    aff.ClusterMerging.forward = checked_merge
+    c = MODEL_CFG
+    L = (c["img_size"] // c["patch_size"]) ** 2
+    keep = int(L * (1 - c["mask_ratio"]))
+    for seed in seeds:
+        torch.manual_seed(seed)
+        g = torch.Generator().manual_seed(seed)
+        model = mae_ref.AFFMaskedAutoEncoder(
+            patch_size=c["patch_size"], img_size=c["img_size"], in_channels=1, mask_ratio=c["mask_ratio"],
+            encoder_embed_dim=list(c["embed_dims"]), encoder_depth=list(c["depths"]),
+            encoder_num_heads=list(c["num_heads"]), encoder_nbhd_size=[48] * 4, cluster_size=8,
+            ds_rate=[0.4] * 4, decoder_embed_dim=c["decoder_dim"], decoder_num_heads=c["decoder_heads"],
+            mlp_ratio=2, merging_method="cluster").eval()
+        imgs = torch.randn((1, 1, c["img_size"], c["img_size"]), generator=g)
+        noise = torch.rand((1, L), generator=g)
+
+        def masking(x, img_size, patch, ratio, noise=noise):
+            ids = noise.argsort(dim=1)
+            return ids[:, :keep], ids[:, keep:].sort(dim=1).values, ids.argsort(dim=1)
+
+        mae_ref.perlin_masking = masking
+        rec["pos"], rec["gaps"] = [], []
+        with torch.no_grad():
+            model.forward_encoder(imgs)
+        print(f"  seed {seed}: stage sizes {[p.shape[1] for p in rec['pos']]}, "
+              f"top-k gaps {['%.1e' % x for x in rec['gaps']]}", flush=True)
+        if min(rec["gaps"]) > 2e-3:
+            break
+    else:
+        raise RuntimeError("no seed with top-k margins")
+    rec["pos"], rec["gaps"] = [], []
+    loss, losses = model(imgs)
+    loss.backward()
+    out = {f"param.{k}": v.detach().numpy() for k, v in model.named_parameters()}
+    out.update({f"grad.{k}": v.grad.detach().numpy() for k, v in model.named_parameters() if v.grad is not None})
+    out.update({f"stage{i}.pos": p.numpy() for i, p in enumerate(rec["pos"])})
+    out.update(images=imgs.numpy(), noise=noise.numpy(), loss=loss.detach().numpy(),
+               losses=torch.stack(losses).detach().numpy(), seed=seed, topk_gap=min(rec["gaps"]))
+    out.update({f"cfg.{k}": np.asarray(v) for k, v in c.items()})
+    np.savez_compressed(HERE / "module_model.npz", **out)
+    print("  wrote module_model.npz", flush=True)
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AFFMAE_REFERENCE"),
                     help="checkout of najafian-lab/affmae (or set AFFMAE_REFERENCE)")
+    ap.add_argument("--only", choices=["modules", "model"], help="generate one of the two groups")
     a = ap.parse_args()
     if not a.reference:
         ap.error("give the reference checkout with --reference or AFFMAE_REFERENCE")
     torch.set_num_threads(1)
     A = load_attention(a.reference)
+    if a.only != "modules":
+        gen_model(a.reference)
+    if a.only == "model":
+        return
     gen_cluster_attention(A)
     gen_deformable(A, A.DeformableCrossAttention, "deform_cross")
     gen_deformable(A, A.DeformableSelfAttention, "deform_self")

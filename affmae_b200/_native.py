@@ -69,6 +69,13 @@ SIGNATURES = {
                                 _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _p],
     "affb_nbhd_build": [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p],
     "affb_token_mask_apply": [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p],
+    "affb_layer_norm_res_fwd": [_p, _i32, _p, _i32, _f32, _u32, _p, _i64, _p, _p, _f32, _i64, _i64, _p, _p, _p,
+                                _p, _p, _p],
+    "affb_layer_norm_res_bwd": [_p, _p, _p, _p, _p, _p, _p, _f32, _u32, _p, _i64, _i64, _i64, _p, _p, _i32, _p,
+                                _p, _p],
+    "affb_sine_embed": [_p, _i64, _i64, _p, _p, _p, _i32, _p],
+    "affb_relu_dropout_fwd": [_p, _i32, _i64, _f32, _u32, _p, _p],
+    "affb_relu_dropout_bwd": [_p, _p, _i32, _i64, _f32, _p, _p],
 }
 OTHER_SYMBOLS = ["affb_last_error", "affb_abi_version", "affb_deform_workspace_bytes",
                  "affb_deform_noalloc_max_scratch_bytes", "affb_nbhd_attn_bwd_workspace_bytes",

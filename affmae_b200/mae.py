@@ -43,6 +43,7 @@ from .kernels.knn import knn
 from .kernels.layer_norm import FusedLayerNorm
 from .kernels.local_attn import FlashLocalAttentionFunction
 from .kernels.pos_bias import pos_bias_gather, rel_pos_bias
+from .kernels.relu_dropout import relu_dropout
 from .kernels.token_mask import apply_token_mask
 from .kernels.weighted_features import weighted_features
 from .workloads import REL_POS_WIDTH, TABLE_WIDTH, relative_position_table
@@ -205,11 +206,16 @@ class DropPath(nn.Module):
         self.p = p
 
     def forward(self, x):
+        f = self.factor(x.shape[0], x.device)
+        return x if f is None else x * f.view((-1,) + (1,) * (x.dim() - 1)).to(x.dtype)
+
+    def factor(self, B: int, device):
+        """Per-sample factor [B] fp32 (0 or 1 / keep), None when inactive; the
+        fused residual norms apply it inside their pass."""
         if not self.training or self.p == 0.0:
-            return x
+            return None
         keep = 1.0 - self.p
-        mask = x.new_empty((x.shape[0],) + (1,) * (x.dim() - 1)).bernoulli_(keep)
-        return x * mask / keep
+        return torch.empty((B,), device=device, dtype=torch.float32).bernoulli_(keep) / keep
 
 
 class ClusterAttention(nn.Module):
@@ -259,12 +265,31 @@ class ClusterBlock(nn.Module):
         self.fc2 = Linear(hidden, dim)
         self.drop_path = DropPath(drop_path)
 
-    def forward(self, feat, member_idx, mask, pe_idx, global_attn: bool = False):
-        # pre-norms feed only Linears: produced directly in the autocast dtype
-        h = self.norm1(feat, out32=False, out16=True)
-        feat = feat + self.drop_path(self.attn(h, member_idx, mask, pe_idx, global_attn))
-        h = self.norm2(feat, out32=False, out16=True)
-        return feat + self.drop_path(self.fc2(F.gelu(self.fc1(h))))
+    def forward(self, feat, member_idx, mask, pe_idx, global_attn: bool = False, pending=None):
+        """Returns (feat, pending): the MLP branch's residual add is left
+        pending, (delta, per-sample factor), so that it runs inside the next
+        block's first norm; ``add_pending`` completes it.  Each residual add
+        with its stochastic-depth factor and the following pre-norm are one
+        fused pass (the norms feed only Linears, so their output is in the
+        autocast dtype)."""
+        B = feat.shape[0]
+        if pending is None:
+            h = self.norm1(feat, out32=False, out16=True)
+        else:
+            feat, h = self.norm1.residual(feat, *pending)
+        a = self.attn(h, member_idx, mask, pe_idx, global_attn)
+        feat, h = self.norm2.residual(feat, a, self.drop_path.factor(B, feat.device))
+        return feat, (self.fc2(F.gelu(self.fc1(h))), self.drop_path.factor(B, feat.device))
+
+
+def add_pending(feat, pending):
+    """feat + factor * delta for a residual add left pending by ClusterBlock."""
+    if pending is None:
+        return feat
+    delta, f = pending
+    if f is not None:
+        delta = delta * f.view((-1,) + (1,) * (delta.dim() - 1)).to(delta.dtype)
+    return feat + delta
 
 
 class ClusterMerging(nn.Module):
@@ -324,8 +349,12 @@ class Stage(nn.Module):
         if global_attn:  # relative indices of every token pair (aff.py:458-459)
             rel = ((pos[:, None, :, :] + REL_POS_WIDTH) - pos[:, :, None, :]).clamp(0, TABLE_WIDTH - 1)
             att_pe = (rel[..., 1] * TABLE_WIDTH + rel[..., 0]).long()
+        pending = None
+        in_dtype = feat.dtype
         for blk in self.blocks:
-            feat = blk(feat, member, mask, att_pe, global_attn)
+            feat, pending = blk(feat, member, mask, att_pe, global_attn, pending)
+        # the fused norms carry the stream in fp32; the stage hands on the dtype it received
+        feat = add_pending(feat, pending).to(in_dtype)
         if self.merge is None:
             return pos, feat, pos, feat
         importance = self.prob_net(feat).sigmoid()
@@ -419,22 +448,31 @@ class Encoder(nn.Module):
 
 # ---------------------------------------------------------------- decoder --
 
-def sine_embedding(pos: torch.Tensor, dim: int) -> torch.Tensor:
+def sine_embedding(pos: torch.Tensor, dim: int, dtype=torch.float32) -> torch.Tensor:
     """[B,n,2] -> [B,n,dim]: sin/cos of x then y, each over dim/2 frequencies,
-    coordinates scaled by 2*pi / max (reference decoder.py:16-62, normalised)."""
+    coordinates scaled by 2*pi / max (reference decoder.py:16-62, normalised).
+    On the GPU one kernel writes it in ``dtype`` with the same fp32 arithmetic."""
     half = dim // 2
+    i = torch.arange(half, device=pos.device, dtype=torch.float32)
+    freq = 10000.0 ** (2 * torch.div(i, 2, rounding_mode="floor") / half)
+    if pos.is_cuda:
+        p = pos.detach().float().contiguous()
+        if p.data_ptr() % 8:
+            p = p.clone()
+        maxes = p.reshape(-1, 2).amax(0).contiguous()
+        out = torch.empty(p.shape[:-1] + (dim,), device=p.device, dtype=dtype)
+        nat.call("affb_sine_embed", nat.ptr(p), p.numel() // 2, dim, nat.ptr(maxes), nat.ptr(freq), nat.ptr(out),
+                 nat.dcode(out), nat.stream(p.device))
+        return out
     x = pos[..., 0].float()
     y = pos[..., 1].float()
     x = x / (x.max() + 1e-6) * (2 * math.pi)
     y = y / (y.max() + 1e-6) * (2 * math.pi)
-    i = torch.arange(half, device=pos.device, dtype=torch.float32)
-    freq = 10000.0 ** (2 * torch.div(i, 2, rounding_mode="floor") / half)
 
     def enc(t):
         t = t[..., None] / freq
         return torch.cat([t[..., 0::2].sin(), t[..., 1::2].cos()], -1)
-    return torch.cat([enc(x), enc(y)], -1)
-
+    return torch.cat([enc(x), enc(y)], -1).to(dtype)
 
 class DeformableAttention(nn.Module):
     """Single-level deformable attention with 4 sampling points per head and
@@ -497,7 +535,9 @@ class DecoderBlock(nn.Module):
         returning both."""
         q, q16 = self._norm(self.norm1, q, self.self_attn(q16, q_pos))
         q, q16 = self._norm(self.norm2, q, self.cross_attn(q16, q_pos, src + src_embed, src_pos))
-        ff = self.linear2(self.drop(F.relu(self.linear1(q16))))
+        h = self.linear1(q16)
+        # ReLU + dropout in one pass; the gradient passes where the output is positive
+        ff = self.linear2(relu_dropout(h, self.p, self.training) if h.is_cuda else self.drop(F.relu(h)))
         return self._norm(self.norm3, q, ff)
 
     def _norm(self, norm, q, delta):
@@ -527,12 +567,12 @@ class PixelDecoder(nn.Module):
                                     for _ in cfg.embed_dims)
 
     def forward(self, stages, queries, q_pos):
-        q = queries + sine_embedding(q_pos, self.dim).to(queries.dtype)
+        q = queries + sine_embedding(q_pos, self.dim, queries.dtype)
         q16 = q
         outs = []
         for proj, blk, (feat, pos) in zip(self.input_proj, self.blocks, reversed(stages)):
             src = proj(feat)
-            q, q16 = blk(q, q16, q_pos, src, pos, sine_embedding(pos, self.dim).to(src.dtype))
+            q, q16 = blk(q, q16, q_pos, src, pos, sine_embedding(pos, self.dim, src.dtype))
             outs.append(q)
         return outs  # coarsest level first
 

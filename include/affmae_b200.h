@@ -181,6 +181,22 @@ int affb_layer_norm_bwd(const float* dy32, const void* dy16_bf16, const void* s,
                         const float* mean, const float* rstd, const float* gamma, float p,
                         uint32_t seed, int64_t R, int64_t C, void* dx, void* ddelta,
                         int delta_dtype, float* dgamma, float* dbeta, void* stream);
+/* Pre-norm residual form (ClusterTransformerBlock, src/layers/aff.py:95-115:
+ * x = x + drop_path(branch); y = norm(x)): s = x + row_scale[r / rows_per_scale]
+ * * dropout_p(delta) (row_scale NULL: factor 1), y = LayerNorm(s).  s is an
+ * fp32 result (the residual stream), not only a saved value.  The backward
+ * takes ds_in, the fp32 gradient of s from its other uses (or NULL), adds the
+ * normalisation's gradient to it and writes dx (fp32) and
+ * ddelta = dx * factor * dropout scale.                                      */
+int affb_layer_norm_res_fwd(const void* x, int x_dtype, const void* delta, int delta_dtype, float p,
+                            uint32_t seed, const float* row_scale, int64_t rows_per_scale,
+                            const float* gamma, const float* beta, float eps, int64_t R, int64_t C,
+                            float* s, float* mean, float* rstd, float* y32, void* y16_bf16, void* stream);
+int affb_layer_norm_res_bwd(const float* dy32, const void* dy16_bf16, const float* ds_in,
+                            const float* s, const float* mean, const float* rstd, const float* gamma,
+                            float p, uint32_t seed, const float* row_scale, int64_t rows_per_scale,
+                            int64_t R, int64_t C, float* dx, void* ddelta, int delta_dtype,
+                            float* dgamma, float* dbeta, void* stream);
 /* Host-side evaluation of that dropout mask: keep[i] = 1 when element e0 + i
  * survives dropout p under `seed` (the kernels' exact rule).  No GPU.  Part
  * of the model glue; the reference uses torch's dropout here.              */
@@ -205,6 +221,24 @@ int affb_nbhd_build(const float* pos, const int64_t* nearest, int64_t B, int64_t
  * gradient (the same product).                                              */
 int affb_token_mask_apply(const void* x, int dtype, int64_t B, int64_t h, int64_t w, int64_t C,
                           const uint8_t* token_mask, int64_t th, int64_t tw, void* out, void* stream);
+
+/* ReLU followed by dropout (the decoder feed-forward network,
+ * src/layers/decoder.py:138-141: dropout3(relu(linear1(x)))) in one pass:
+ * y[e] = (x[e] > 0 and keep(seed, e)) ? x[e] / (1 - p) : 0 over n elements,
+ * keep() being the same Philox-4x32-10 stream as affb_dropout_keep_mask; p = 0
+ * gives a plain ReLU.  The gradient needs no mask: dx = (y > 0) ? dy / (1 - p)
+ * : 0.  x, y, dy, dx: n elements of dtype. */
+/* Normalised sine position embedding (PositionEmbeddingSine,
+ * src/layers/decoder.py:16-62, normalize=True): pos [R,2] fp32 -> out [R,D]
+ * of dtype, out = [sin(u_x[0::2]), cos(u_x[1::2]), sin(u_y[0::2]),
+ * cos(u_y[1::2])] with u = coord / (maxes[axis] + 1e-6) * 2pi / freq;
+ * maxes [2] (device, fp32) are the coordinate maxima over all rows, freq
+ * [D/2] (device, fp32) the frequency table.  D a multiple of 4. */
+int affb_sine_embed(const float* pos, int64_t R, int64_t D, const float* maxes, const float* freq, void* out,
+                    int dtype, void* stream);
+
+int affb_relu_dropout_fwd(const void* x, int dtype, int64_t n, float p, uint32_t seed, void* y, void* stream);
+int affb_relu_dropout_bwd(const void* dy, const void* y, int dtype, int64_t n, float p, void* dx, void* stream);
 
 /* --------------------------------- fused KNN deformable attention (2-D) --
  * Replaces fused_knn_deform_cross_attn_forward_save

@@ -564,7 +564,7 @@ def test_rel_pos_bias_matches_table_gather(cuda, dtype):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("C", [48, 96, 384, 1536])
+@pytest.mark.parametrize("C", [48, 96, 192, 320, 384, 1536])
 def test_fused_layer_norm_matches_torch(cuda, xdtype, C):
     """LayerNorm(x) with fp32 and bf16 outputs, values and all gradients, against
     torch.nn.functional.layer_norm in fp32."""
@@ -614,6 +614,41 @@ def test_fused_residual_dropout_layer_norm(cuda, p):
     rx, rd = torch.autograd.grad(ref, (xr, dr), gy)
     assert rel_err(dx.cpu(), rx.cpu()) < 1e-4
     assert rel_err(dd.float().cpu(), rd.cpu()) < 8e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("scaled", [False, True])
+@pytest.mark.parametrize("with_ds", [False, True])
+def test_residual_layer_norm_pre_norm_form(cuda, scaled, with_ds):
+    """(s, y) = (x + f_b * delta, LayerNorm(s)) with a per-sample factor f_b
+    (stochastic depth; 0 for one sample) against the torch sequence in fp32;
+    the backward with and without a gradient of s from its other uses."""
+    from affmae_b200.kernels.layer_norm import ResidualNormFunction
+    g = torch.Generator().manual_seed(7)
+    B, N, C = 3, 211, 384
+    x = torch.randn((B, N, C), generator=g).to(cuda).requires_grad_(True)
+    d = torch.randn((B, N, C), generator=g).to(cuda, torch.bfloat16).requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(C, generator=g)).to(cuda).requires_grad_(True)
+    b = (0.1 * torch.randn(C, generator=g)).to(cuda).requires_grad_(True)
+    f = torch.tensor([1 / 0.9, 0.0, 1 / 0.9], device=cuda) if scaled else None
+    s, y = ResidualNormFunction.apply(x, d, f, w, b, 1e-5)
+    xr = x.detach().clone().requires_grad_(True)
+    dr = d.detach().float().clone().requires_grad_(True)
+    sr = xr + dr * (f.view(B, 1, 1) if scaled else 1.0)
+    yr = torch.nn.functional.layer_norm(sr, (C,), w, b, 1e-5)
+    assert rel_err(s.detach().cpu(), sr.detach().cpu()) < 1e-6
+    assert rel_err(y.float().detach().cpu(), yr.detach().cpu()) < 8e-3
+    gy = torch.randn(y.shape, generator=g).to(cuda, torch.bfloat16)
+    gs = torch.randn(s.shape, generator=g).to(cuda) if with_ds else None
+    outs, grads = ((s, y), (gs, gy)) if with_ds else ((y,), (gy,))
+    dx, dd, dw, db = torch.autograd.grad(outs, (x, d, w, b), grads)
+    routs, rgrads = ((sr, yr), (gs, gy.float())) if with_ds else ((yr,), (gy.float(),))
+    rx, rd, rw, rb = torch.autograd.grad(routs, (xr, dr, w, b), rgrads)
+    assert rel_err(dx.cpu(), rx.cpu()) < 1e-4
+    assert rel_err(dd.float().cpu(), rd.cpu()) < 8e-3
+    if scaled:
+        assert bool((dd[1] == 0).all())
+    assert rel_err(dw.cpu(), rw.cpu()) < 1e-4 and rel_err(db.cpu(), rb.cpu()) < 1e-4
 
 
 @pytest.mark.gpu

@@ -191,13 +191,17 @@ class _LinearFunction(torch.autograd.Function):
         return dx, dw, db
 
 
+def _linear(x, weight, bias):
+    if x.is_cuda and torch.is_autocast_enabled("cuda"):
+        return _LinearFunction.apply(x, weight, bias)
+    return F.linear(x, weight, bias)
+
+
 class Linear(nn.Linear):
     """nn.Linear whose CUDA autocast path runs through _LinearFunction."""
 
     def forward(self, x):
-        if x.is_cuda and torch.is_autocast_enabled("cuda"):
-            return _LinearFunction.apply(x, self.weight, self.bias)
-        return F.linear(x, self.weight, self.bias)
+        return _linear(x, self.weight, self.bias)
 
 
 class DropPath(nn.Module):
@@ -503,8 +507,12 @@ class DeformableAttention(nn.Module):
     def forward(self, query, query_pos, kv=None, kv_pos=None):
         B, n, C = query.shape
         H, P = self.heads, self.points
-        off = self.sampling_offsets(query).view(B, n, H, P, 2)
-        aw = F.softmax(self.attention_weights(query).view(B, n, H, P), dim=-1)
+        # sampling offsets and attention weights read the same input: one GEMM
+        # over the two weight matrices stacked (one input gradient, not two summed)
+        ow = _linear(query, torch.cat([self.sampling_offsets.weight, self.attention_weights.weight]),
+                     torch.cat([self.sampling_offsets.bias, self.attention_weights.bias]))
+        off = ow[..., :H * P * 2].view(B, n, H, P, 2)
+        aw = F.softmax(ow[..., H * P * 2:].view(B, n, H, P), dim=-1)
         if kv is None:  # self attention
             vals = self.value_proj(query).view(B, n, H, C // H)
             out = fused_knn_deformable_self_attention(query_pos, off, aw, vals, self.shepard_power)
@@ -568,10 +576,13 @@ class PixelDecoder(nn.Module):
 
     def forward(self, stages, queries, q_pos):
         q = queries + sine_embedding(q_pos, self.dim, queries.dtype)
-        q16 = q
+        # the Linears' input in the autocast dtype once, not a cast inside each of them
+        amp = q.is_cuda and torch.is_autocast_enabled("cuda")
+        q16 = q.to(torch.get_autocast_dtype("cuda")) if amp else q
         outs = []
         for proj, blk, (feat, pos) in zip(self.input_proj, self.blocks, reversed(stages)):
-            src = proj(feat)
+            # the projected level only feeds value projections: normalised straight into bf16
+            src = proj[1](proj[0](feat), out32=False, out16=True)
             q, q16 = blk(q, q16, q_pos, src, pos, sine_embedding(pos, self.dim, src.dtype))
             outs.append(q)
         return outs  # coarsest level first

@@ -31,6 +31,19 @@ namespace affb {
 
 constexpr int DK_WARPS = 8;
 constexpr int DK_SMAX = 64;  // samples per query (H * 4) handled per warp
+constexpr int DK_FWD_SLOTS = 128;  // forward: samples of the queries a warp handles together
+
+// Queries per warp in the forward: with H * 4 samples per query not a
+// multiple of 32 (6 heads: 24) one query leaves lanes idle in both the search
+// (one sample per lane) and the gather (one 8-channel chunk per lane), so a
+// warp takes several consecutive queries and deals their samples and chunks
+// out over its lanes (6 heads: 4 queries, 96 samples and 192 chunks, every
+// lane busy).
+static int deform_fwd_queries_per_warp(int S) {
+  int q = 1;
+  while (q < 4 && (q * S) % 32 != 0 && 2 * q * S <= DK_FWD_SLOTS) q *= 2;
+  return q;
+}
 
 // ---------------------------------------------------------------- grid build
 __global__ void grid_bbox_kernel(const float* __restrict__ pos, int64_t nkv, int G,
@@ -193,22 +206,29 @@ __global__ void __launch_bounds__(DK_WARPS * 32)
 deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ offsets,
                       const float* __restrict__ attn_w, const T* __restrict__ values,
                       const float* __restrict__ power, int64_t B, int64_t Nq, int64_t Nkv, int H,
-                      int C, GridView gv, T* __restrict__ out, int32_t* __restrict__ knn_idx,
+                      int C, int qpw, GridView gv, T* __restrict__ out, int32_t* __restrict__ knn_idx,
                       float* __restrict__ knn_d2) {
-  __shared__ int s_idx[DK_WARPS][DK_SMAX * 4];
-  __shared__ float s_w[DK_WARPS][DK_SMAX * 4];
-  __shared__ float s_aw[DK_WARPS][DK_SMAX];
+  // per warp: slots = qpw * H * 4 samples of (4 indices, 4 weights, 1 attention weight);
+  // sized to the launch so the rest of the SM's shared/L1 storage caches the grid
+  extern __shared__ int dk_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t gq = (int64_t)blockIdx.x * DK_WARPS + warp;
-  if (gq >= B * Nq) return;
-  const int64_t b = gq / Nq;
+  const int slots = qpw * H * 4;
+  int* s_idx = dk_smem + warp * slots * 9;
+  float* s_w = reinterpret_cast<float*>(s_idx + slots * 4);
+  float* s_aw = s_w + slots * 4;
+  const int64_t gq0 = ((int64_t)blockIdx.x * DK_WARPS + warp) * qpw;   // first query of this warp
+  if (gq0 >= B * Nq) return;
+  const int nq = (int)(B * Nq - gq0 < qpw ? B * Nq - gq0 : qpw);
   const float P = fmaxf(power[0], 1e-6f);
-  const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
   const int S = H * 4;
-  for (int s = lane; s < S; s += 32) {
-    const int64_t gs = gq * S + s;
-    const float sx = __fadd_rn(qx, offsets[2 * gs]);
-    const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
+  // search: lane t takes sample t % S of query t / S
+  for (int t = lane; t < nq * S; t += 32) {
+    const int qi = t / S;
+    const int64_t gq = gq0 + qi;
+    const int64_t b = gq / Nq;
+    const int64_t gs = gq0 * S + t;
+    const float sx = __fadd_rn(qpos[2 * gq], offsets[2 * gs]);
+    const float sy = __fadd_rn(qpos[2 * gq + 1], offsets[2 * gs + 1]);
     Top4 top;
     grid_knn4(gv, b, sx, sy, top);
     reinterpret_cast<int4*>(knn_idx)[gs] = make_int4(top.i[0], top.i[1], top.i[2], top.i[3]);
@@ -217,35 +237,39 @@ deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     shepard4(top.d, P, w, dist);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      s_idx[warp][s * 4 + j] = top.i[j];
-      s_w[warp][s * 4 + j] = w[j];
+      s_idx[t * 4 + j] = top.i[j];
+      s_w[t * 4 + j] = w[j];
     }
-    s_aw[warp][s] = attn_w[gs];
+    s_aw[t] = attn_w[gs];
   }
   __syncwarp();
+  // gather: lane t takes 8-channel chunk t % (H*C/8) of query t / (H*C/8)
   const int row = H * C;
-  const T* vb = values + b * Nkv * row;
-  for (int c8 = lane; c8 * 8 < row; c8 += 32) {
+  const int nc8 = row / 8;
+  for (int t = lane; t < nq * nc8; t += 32) {
+    const int qi = t / nc8, c8 = t - qi * nc8;
+    const int64_t gq = gq0 + qi;
+    const T* vb = values + (gq / Nq) * Nkv * row;
     const int h = (c8 * 8) / C;
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      const int si = h * 4 + p;
+      const int si = qi * S + h * 4 + p;
       float wv[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) wv[e] = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int id = s_idx[warp][si * 4 + j];
-        const float w = s_w[warp][si * 4 + j];
+        const int id = s_idx[si * 4 + j];
+        const float w = s_w[si * 4 + j];
         float v[8];
         ld8(vb + (int64_t)id * row + c8 * 8, v);
 #pragma unroll
         for (int e = 0; e < 8; ++e) wv[e] = fmaf(w, v[e], wv[e]);
       }
-      const float aw = s_aw[warp][si];
+      const float aw = s_aw[si];
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = fmaf(aw, wv[e], acc[e]);
     }
@@ -291,16 +315,22 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
                       float* __restrict__ d_off, float* __restrict__ d_aw,
                       float* __restrict__ d_qpos, float* __restrict__ d_kvpos,
                       float* __restrict__ d_val, float* __restrict__ d_power) {
-  __shared__ int s_idx[DK_WARPS][DK_SMAX * 4];
-  __shared__ int s_first[DK_WARPS][DK_SMAX * 4];   // first entry of the head with the same kv row
-  __shared__ float s_w[DK_WARPS][DK_SMAX * 4];
-  __shared__ float s_cf[DK_WARPS][DK_SMAX * 4];    // merged aw * w of a first entry
-  __shared__ float s_dot[DK_WARPS][DK_SMAX * 4];   // v[row] . dout[head] of a first entry
-  __shared__ float s_aw[DK_WARPS][DK_SMAX];
+  // per warp, for its query's S = H * 4 samples (sized to the launch so the rest
+  // of the SM's shared/L1 storage caches values and positions):
+  //   s_idx, s_first (first entry of the head with the same kv row), s_w,
+  //   s_cf (merged aw * w of a first entry), s_dot (v[row] . dout[head] of a
+  //   first entry): S * 4 each; s_aw: S
   __shared__ float s_pow[DK_WARPS];
+  extern __shared__ int dkb_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float P = fmaxf(power[0], 1e-6f);
   const int S = H * 4;
+  int* s_idx = dkb_smem + warp * S * 21;
+  int* s_first = s_idx + S * 4;
+  float* s_w = reinterpret_cast<float*>(s_first + S * 4);
+  float* s_cf = s_w + S * 4;
+  float* s_dot = s_cf + S * 4;
+  float* s_aw = s_dot + S * 4;
   const int row = H * C;
   const int nc8 = row / 8;
   const int G = C / 8;  // lanes (8-channel chunks) per head
@@ -318,21 +348,21 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
-      s_idx[warp][s * 4 + 0] = ii.x; s_idx[warp][s * 4 + 1] = ii.y;
-      s_idx[warp][s * 4 + 2] = ii.z; s_idx[warp][s * 4 + 3] = ii.w;
+      s_idx[s * 4 + 0] = ii.x; s_idx[s * 4 + 1] = ii.y;
+      s_idx[s * 4 + 2] = ii.z; s_idx[s * 4 + 3] = ii.w;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { s_w[warp][s * 4 + j] = w[j]; s_cf[warp][s * 4 + j] = 0.f; s_dot[warp][s * 4 + j] = 0.f; }
-      s_aw[warp][s] = attn_w[gs];
+      for (int j = 0; j < 4; ++j) { s_w[s * 4 + j] = w[j]; s_cf[s * 4 + j] = 0.f; s_dot[s * 4 + j] = 0.f; }
+      s_aw[s] = attn_w[gs];
     }
     __syncwarp();
     // merge entries of a head that name the same kv row
     for (int t = lane; t < S * 4; t += 32) {
-      const int h0 = (t >> 4) << 4, id = s_idx[warp][t];
+      const int h0 = (t >> 4) << 4, id = s_idx[t];
       int f = t;
       for (int u = h0; u < t; ++u)
-        if (s_idx[warp][u] == id) { f = u; break; }
-      s_first[warp][t] = f;
-      atomicAdd(&s_cf[warp][f], s_aw[warp][t >> 2] * s_w[warp][t]);
+        if (s_idx[u] == id) { f = u; break; }
+      s_first[t] = f;
+      atomicAdd(&s_cf[f], s_aw[t >> 2] * s_w[t]);
     }
     __syncwarp();
     const T* vb = values + b * Nkv * row;
@@ -349,31 +379,31 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       }
       for (int k = 0; k < 16; ++k) {
         const int t = h * 16 + k;
-        const bool first = act && s_first[warp][t] == t;
+        const bool first = act && s_first[t] == t;
         float dot = 0.f;
         if (first) {
-          const int id = s_idx[warp][t];
+          const int id = s_idx[t];
           float v[8];
           ld8(vb + (int64_t)id * row + c8 * 8, v);
 #pragma unroll
           for (int e = 0; e < 8; ++e) dot = fmaf(v[e], g[e], dot);
-          const float cf = s_cf[warp][t];
+          const float cf = s_cf[t];
           float* dst = dvb + (int64_t)id * row + c8 * 8;
           red_add_v4(dst, cf * g[0], cf * g[1], cf * g[2], cf * g[3]);
           red_add_v4(dst + 4, cf * g[4], cf * g[5], cf * g[6], cf * g[7]);
         }
         if (shfl) {
           for (int o = G >> 1; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (first && (lane % G) == 0) s_dot[warp][t] = dot;
+          if (first && (lane % G) == 0) s_dot[t] = dot;
         } else if (first) {
-          atomicAdd(&s_dot[warp][t], dot);
+          atomicAdd(&s_dot[t], dot);
         }
       }
     }
     __syncwarp();
     // d_kv_pos is summed per distinct kv row of a head in shared memory (in
     // s_w / s_cf, no longer read) and scattered once per row below
-    for (int t = lane; t < S * 4; t += 32) { s_w[warp][t] = 0.f; s_cf[warp][t] = 0.f; }
+    for (int t = lane; t < S * 4; t += 32) { s_w[t] = 0.f; s_cf[t] = 0.f; }
     __syncwarp();
     float gqx = 0.f, gqy = 0.f;
     float* dkvb = d_kvpos + b * Nkv * 2;
@@ -381,17 +411,17 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       const int64_t gs = gq * S + s;
       const float sx = __fadd_rn(qx, offsets[2 * gs]);
       const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
-      const int4 ii = make_int4(s_idx[warp][s * 4], s_idx[warp][s * 4 + 1], s_idx[warp][s * 4 + 2],
-                                s_idx[warp][s * 4 + 3]);
+      const int4 ii = make_int4(s_idx[s * 4], s_idx[s * 4 + 1], s_idx[s * 4 + 2],
+                                s_idx[s * 4 + 3]);
       float d2[4];
       load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
-      const float aw = s_aw[warp][s];
+      const float aw = s_aw[s];
       float dot[4], datt = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        dot[j] = s_dot[warp][s_first[warp][s * 4 + j]];
+        dot[j] = s_dot[s_first[s * 4 + j]];
         datt = fmaf(w[j], dot[j], datt);
       }
       d_aw[gs] = datt;
@@ -404,13 +434,13 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
         const float ds = w[j] * (dp[j] - wdp);
         dpow += ds * (-dist[j]);
         const float dd2 = (ds * (-P)) / (2.f * dist[j]);
-        const int id = s_idx[warp][s * 4 + j];
+        const int id = s_idx[s * 4 + j];
         const float ex = sx - kvb[2 * id], ey = sy - kvb[2 * id + 1];
         dsx = fmaf(ex, dd2, dsx);
         dsy = fmaf(ey, dd2, dsy);
-        const int f = s_first[warp][s * 4 + j];
-        atomicAdd(&s_w[warp][f], -2.f * ex * dd2);
-        atomicAdd(&s_cf[warp][f], -2.f * ey * dd2);
+        const int f = s_first[s * 4 + j];
+        atomicAdd(&s_w[f], -2.f * ex * dd2);
+        atomicAdd(&s_cf[f], -2.f * ey * dd2);
       }
       dsx *= 2.f;
       dsy *= 2.f;
@@ -421,10 +451,10 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     }
     __syncwarp();
     for (int t = lane; t < S * 4; t += 32) {
-      if (s_first[warp][t] != t) continue;
-      const int id = s_idx[warp][t];
-      red_add(dkvb + 2 * id, s_w[warp][t]);
-      red_add(dkvb + 2 * id + 1, s_cf[warp][t]);
+      if (s_first[t] != t) continue;
+      const int id = s_idx[t];
+      red_add(dkvb + 2 * id, s_w[t]);
+      red_add(dkvb + 2 * id + 1, s_cf[t]);
     }
     gqx = warp_sum(gqx);
     gqy = warp_sum(gqy);
@@ -477,11 +507,13 @@ extern "C" int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos,
   cudaStream_t st = as_stream(stream);
   GridView gv;
   if (int e = build_grid(kv_pos, B, Nkv, workspace, gv, st)) return e;
-  const unsigned nb = (unsigned)((B * Nq + DK_WARPS - 1) / DK_WARPS);
+  const int qpw = deform_fwd_queries_per_warp((int)H * 4);
+  const unsigned nb = (unsigned)((B * Nq + DK_WARPS * qpw - 1) / (DK_WARPS * qpw));
+  const size_t smem = (size_t)DK_WARPS * qpw * H * 4 * 9 * sizeof(int);
   AFFB_DISPATCH(dtype, T,
-                deform_knn_fwd_kernel<T><<<nb, DK_WARPS * 32, 0, st>>>(
+                deform_knn_fwd_kernel<T><<<nb, DK_WARPS * 32, smem, st>>>(
                     query_pos, offsets, attn_w, (const T*)values, power, B, Nq, Nkv, (int)H,
-                    (int)C, gv, (T*)out, knn_idx, knn_d2));
+                    (int)C, qpw, gv, (T*)out, knn_idx, knn_d2));
   AFFB_LAUNCH_CHECK("affb_deform_knn_fwd");
   return AFFB_OK;
 }
@@ -503,7 +535,7 @@ extern "C" int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos,
   const int64_t need = (B * Nq + DK_WARPS - 1) / DK_WARPS;
   const unsigned nb = (unsigned)imin64(need, (int64_t)sm_count() * 8);
   AFFB_DISPATCH(dtype, T,
-                deform_knn_bwd_kernel<T><<<nb, DK_WARPS * 32, 0, st>>>(
+                deform_knn_bwd_kernel<T><<<nb, DK_WARPS * 32, (size_t)DK_WARPS * H * 4 * 21 * sizeof(int), st>>>(
                     query_pos, kv_pos, offsets, attn_w, (const T*)values, power, knn_idx, knn_d2,
                     (const T*)dout, B, Nq, Nkv, (int)H, (int)C, d_offsets, d_attn_w, d_qpos,
                     d_kvpos, d_values_acc, d_power));

@@ -30,6 +30,21 @@
 namespace affb {
 
 constexpr int DK_WARPS = 8;
+// Block shapes: warps per block and the minimum resident blocks asked of the
+// register allocator.  The forward's grid search is latency bound (waits on
+// cell ranges and points in L1/L2), so residency is what hides it: at 5 blocks
+// of 8 warps (48 registers, a few bytes spilled) config 4's forward + backward
+// take 2.21 ms against 2.36 at 64 registers (4 blocks) and 3.57 at 100 (2).
+#ifndef AFFB_DKF_WARPS
+#define AFFB_DKF_WARPS 8
+#endif
+#ifndef AFFB_DKF_MINB
+#define AFFB_DKF_MINB 5
+#endif
+#ifndef AFFB_DKB_MINB
+#define AFFB_DKB_MINB 4
+#endif
+constexpr int DKF_WARPS = AFFB_DKF_WARPS;
 constexpr int DK_SMAX = 64;  // samples per query (H * 4) handled per warp
 constexpr int DK_FWD_SLOTS = 128;  // forward: samples of the queries a warp handles together
 
@@ -202,7 +217,7 @@ __device__ __forceinline__ void shepard4(const float* d2, float P, float* w, flo
 }
 
 template <typename T>
-__global__ void __launch_bounds__(DK_WARPS * 32)
+__global__ void __launch_bounds__(DKF_WARPS * 32, AFFB_DKF_MINB)
 deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ offsets,
                       const float* __restrict__ attn_w, const T* __restrict__ values,
                       const float* __restrict__ power, int64_t B, int64_t Nq, int64_t Nkv, int H,
@@ -216,7 +231,7 @@ deform_knn_fwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
   int* s_idx = dk_smem + warp * slots * 9;
   float* s_w = reinterpret_cast<float*>(s_idx + slots * 4);
   float* s_aw = s_w + slots * 4;
-  const int64_t gq0 = ((int64_t)blockIdx.x * DK_WARPS + warp) * qpw;   // first query of this warp
+  const int64_t gq0 = ((int64_t)blockIdx.x * DKF_WARPS + warp) * qpw;   // first query of this warp
   if (gq0 >= B * Nq) return;
   const int nq = (int)(B * Nq - gq0 < qpw ? B * Nq - gq0 : qpw);
   const float P = fmaxf(power[0], 1e-6f);
@@ -306,7 +321,7 @@ __device__ __forceinline__ void load_d2(const float* __restrict__ knn_d2, int64_
 // chunks form an aligned lane group (C/8 divides 32), else with shared-memory
 // atomics.
 template <typename T>
-__global__ void __launch_bounds__(DK_WARPS * 32)
+__global__ void __launch_bounds__(DK_WARPS * 32, AFFB_DKB_MINB)
 deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ kvpos,
                       const float* __restrict__ offsets, const float* __restrict__ attn_w,
                       const T* __restrict__ values, const float* __restrict__ power,
@@ -508,10 +523,10 @@ extern "C" int affb_deform_knn_fwd(const float* query_pos, const float* kv_pos,
   GridView gv;
   if (int e = build_grid(kv_pos, B, Nkv, workspace, gv, st)) return e;
   const int qpw = deform_fwd_queries_per_warp((int)H * 4);
-  const unsigned nb = (unsigned)((B * Nq + DK_WARPS * qpw - 1) / (DK_WARPS * qpw));
-  const size_t smem = (size_t)DK_WARPS * qpw * H * 4 * 9 * sizeof(int);
+  const unsigned nb = (unsigned)((B * Nq + DKF_WARPS * qpw - 1) / (DKF_WARPS * qpw));
+  const size_t smem = (size_t)DKF_WARPS * qpw * H * 4 * 9 * sizeof(int);
   AFFB_DISPATCH(dtype, T,
-                deform_knn_fwd_kernel<T><<<nb, DK_WARPS * 32, smem, st>>>(
+                deform_knn_fwd_kernel<T><<<nb, DKF_WARPS * 32, smem, st>>>(
                     query_pos, offsets, attn_w, (const T*)values, power, B, Nq, Nkv, (int)H,
                     (int)C, qpw, gv, (T*)out, knn_idx, knn_d2));
   AFFB_LAUNCH_CHECK("affb_deform_knn_fwd");

@@ -312,7 +312,10 @@ __device__ __forceinline__ void load_d2(const float* __restrict__ knn_d2, int64_
   }
 }
 
-// Backward, one warp per query.  Per head the 4 points x 4 neighbours give 16
+// Backward, qpw consecutive queries per warp (several when one query's
+// 8-channel chunks, H * C / 8, do not fill whole passes of 32 lanes: 6 heads
+// of 64 channels give 48 chunks, so 2 queries give 3 full passes instead of
+// 2 passes at 75 %).  Per head the 4 points x 4 neighbours give 16
 // (kv row, coefficient aw * w) entries; entries naming the same kv row are
 // merged first (neighbouring sampling points share neighbours), so each
 // distinct row is gathered once for the dot products and receives one
@@ -320,7 +323,7 @@ __device__ __forceinline__ void load_d2(const float* __restrict__ knn_d2, int64_
 // are reduced over the head's lanes with shuffles when a head's 8-channel
 // chunks form an aligned lane group (C/8 divides 32), else with shared-memory
 // atomics.
-template <typename T>
+template <typename T, int QPW>
 __global__ void __launch_bounds__(DK_WARPS * 32, AFFB_DKB_MINB)
 deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ kvpos,
                       const float* __restrict__ offsets, const float* __restrict__ attn_w,
@@ -330,48 +333,53 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
                       float* __restrict__ d_off, float* __restrict__ d_aw,
                       float* __restrict__ d_qpos, float* __restrict__ d_kvpos,
                       float* __restrict__ d_val, float* __restrict__ d_power) {
-  // per warp, for its query's S = H * 4 samples (sized to the launch so the rest
-  // of the SM's shared/L1 storage caches values and positions):
-  //   s_idx, s_first (first entry of the head with the same kv row), s_w,
-  //   s_cf (merged aw * w of a first entry), s_dot (v[row] . dout[head] of a
-  //   first entry): S * 4 each; s_aw: S
+  // per warp, for the slots = qpw * H * 4 samples of its queries (sized to the
+  // launch so the rest of the SM's shared/L1 storage caches values and
+  // positions): s_idx, s_first (first entry of the head with the same kv row),
+  // s_w, s_cf (merged aw * w of a first entry), s_dot (v[row] . dout[head] of
+  // a first entry): slots * 4 each; s_aw: slots
   __shared__ float s_pow[DK_WARPS];
   extern __shared__ int dkb_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float P = fmaxf(power[0], 1e-6f);
   const int S = H * 4;
-  int* s_idx = dkb_smem + warp * S * 21;
-  int* s_first = s_idx + S * 4;
-  float* s_w = reinterpret_cast<float*>(s_first + S * 4);
-  float* s_cf = s_w + S * 4;
-  float* s_dot = s_cf + S * 4;
-  float* s_aw = s_dot + S * 4;
+  constexpr int qpw = QPW;
+  const int slots = qpw * S;
+  int* s_idx = dkb_smem + warp * slots * 21;
+  int* s_first = s_idx + slots * 4;
+  float* s_w = reinterpret_cast<float*>(s_first + slots * 4);
+  float* s_cf = s_w + slots * 4;
+  float* s_dot = s_cf + slots * 4;
+  float* s_aw = s_dot + slots * 4;
   const int row = H * C;
   const int nc8 = row / 8;
   const int G = C / 8;  // lanes (8-channel chunks) per head
   const bool shfl = G <= 32 && (32 % G) == 0;
   float dpow = 0.f;
-  for (int64_t gq = (int64_t)blockIdx.x * DK_WARPS + warp; gq < B * Nq;
-       gq += (int64_t)gridDim.x * DK_WARPS) {
-    const int64_t b = gq / Nq;
-    const float* kvb = kvpos + b * Nkv * 2;
-    const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
-    for (int s = lane; s < S; s += 32) {
-      const int64_t gs = gq * S + s;
+  const int64_t nqtot = B * Nq;
+  for (int64_t gq0 = ((int64_t)blockIdx.x * DK_WARPS + warp) * qpw; gq0 < nqtot;
+       gq0 += (int64_t)gridDim.x * DK_WARPS * qpw) {
+    const int nq = (int)(nqtot - gq0 < qpw ? nqtot - gq0 : qpw);
+    // sample slot t = qi * S + h * 4 + p of query gq0 + qi
+    for (int t = lane; t < nq * S; t += 32) {
+      const int64_t gq = gq0 + (QPW == 1 ? 0 : t / S);
+      const float* kvb = kvpos + (gq / Nq) * Nkv * 2;
+      const int64_t gs = gq0 * S + t;
       const int4 ii = reinterpret_cast<const int4*>(knn_idx)[gs];
       float d2[4];
-      load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
+      load_d2(knn_d2, gs, ii, kvb, qpos[2 * gq], qpos[2 * gq + 1], offsets, d2);
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
-      s_idx[s * 4 + 0] = ii.x; s_idx[s * 4 + 1] = ii.y;
-      s_idx[s * 4 + 2] = ii.z; s_idx[s * 4 + 3] = ii.w;
+      s_idx[t * 4 + 0] = ii.x; s_idx[t * 4 + 1] = ii.y;
+      s_idx[t * 4 + 2] = ii.z; s_idx[t * 4 + 3] = ii.w;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { s_w[s * 4 + j] = w[j]; s_cf[s * 4 + j] = 0.f; s_dot[s * 4 + j] = 0.f; }
-      s_aw[s] = attn_w[gs];
+      for (int j = 0; j < 4; ++j) { s_w[t * 4 + j] = w[j]; s_cf[t * 4 + j] = 0.f; s_dot[t * 4 + j] = 0.f; }
+      s_aw[t] = attn_w[gs];
     }
     __syncwarp();
-    // merge entries of a head that name the same kv row
-    for (int t = lane; t < S * 4; t += 32) {
+    // merge entries of a head that name the same kv row (entry e = slot * 4 + j;
+    // the 16 entries of one head of one query are e >> 4)
+    for (int t = lane; t < nq * S * 4; t += 32) {
       const int h0 = (t >> 4) << 4, id = s_idx[t];
       int f = t;
       for (int u = h0; u < t; ++u)
@@ -380,20 +388,26 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       atomicAdd(&s_cf[f], s_aw[t >> 2] * s_w[t]);
     }
     __syncwarp();
-    const T* vb = values + b * Nkv * row;
-    float* dvb = d_val + b * Nkv * row;
-    for (int base = 0; base < nc8; base += 32) {
-      const int c8 = base + lane;
-      const bool act = c8 < nc8;
-      const int h = act ? (c8 * 8) / C : 0;
+    // chunk u = qi * nc8 + c8; a head's G chunks stay in one aligned lane group
+    for (int base = 0; base < nq * nc8; base += 32) {
+      const int u = base + lane;
+      const bool act = u < nq * nc8;
+      const int qi = (QPW == 1 || !act) ? 0 : u / nc8;
+      const int c8 = act ? u - qi * nc8 : 0;
+      const int h = (c8 * 8) / C;
+      const int64_t gq = gq0 + qi;
+      const int64_t b = gq / Nq;
+      const T* vb = values + b * Nkv * row;
+      float* dvb = d_val + b * Nkv * row;
       float g[8];
       if (act) ld8(dout + gq * row + c8 * 8, g);
       else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) g[e] = 0.f;
       }
+      const int e0 = (qi * H + h) * 16;
       for (int k = 0; k < 16; ++k) {
-        const int t = h * 16 + k;
+        const int t = e0 + k;
         const bool first = act && s_first[t] == t;
         float dot = 0.f;
         if (first) {
@@ -418,25 +432,29 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     __syncwarp();
     // d_kv_pos is summed per distinct kv row of a head in shared memory (in
     // s_w / s_cf, no longer read) and scattered once per row below
-    for (int t = lane; t < S * 4; t += 32) { s_w[t] = 0.f; s_cf[t] = 0.f; }
+    for (int t = lane; t < nq * S * 4; t += 32) { s_w[t] = 0.f; s_cf[t] = 0.f; }
     __syncwarp();
-    float gqx = 0.f, gqy = 0.f;
-    float* dkvb = d_kvpos + b * Nkv * 2;
-    for (int s = lane; s < S; s += 32) {
-      const int64_t gs = gq * S + s;
+    float gqx[QPW], gqy[QPW];   // this lane's share of d_query_pos per query
+#pragma unroll
+    for (int i = 0; i < QPW; ++i) { gqx[i] = 0.f; gqy[i] = 0.f; }
+    for (int t = lane; t < nq * S; t += 32) {
+      const int qi = QPW == 1 ? 0 : t / S;
+      const int64_t gq = gq0 + qi;
+      const float* kvb = kvpos + (gq / Nq) * Nkv * 2;
+      const float qx = qpos[2 * gq], qy = qpos[2 * gq + 1];
+      const int64_t gs = gq0 * S + t;
       const float sx = __fadd_rn(qx, offsets[2 * gs]);
       const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
-      const int4 ii = make_int4(s_idx[s * 4], s_idx[s * 4 + 1], s_idx[s * 4 + 2],
-                                s_idx[s * 4 + 3]);
+      const int4 ii = make_int4(s_idx[t * 4], s_idx[t * 4 + 1], s_idx[t * 4 + 2], s_idx[t * 4 + 3]);
       float d2[4];
       load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
       float w[4], dist[4];
       shepard4(d2, P, w, dist);
-      const float aw = s_aw[s];
+      const float aw = s_aw[t];
       float dot[4], datt = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        dot[j] = s_dot[s_first[s * 4 + j]];
+        dot[j] = s_dot[s_first[t * 4 + j]];
         datt = fmaf(w[j], dot[j], datt);
       }
       d_aw[gs] = datt;
@@ -449,11 +467,11 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
         const float ds = w[j] * (dp[j] - wdp);
         dpow += ds * (-dist[j]);
         const float dd2 = (ds * (-P)) / (2.f * dist[j]);
-        const int id = s_idx[s * 4 + j];
+        const int id = s_idx[t * 4 + j];
         const float ex = sx - kvb[2 * id], ey = sy - kvb[2 * id + 1];
         dsx = fmaf(ex, dd2, dsx);
         dsy = fmaf(ey, dd2, dsy);
-        const int f = s_first[s * 4 + j];
+        const int f = s_first[t * 4 + j];
         atomicAdd(&s_w[f], -2.f * ex * dd2);
         atomicAdd(&s_cf[f], -2.f * ey * dd2);
       }
@@ -461,21 +479,25 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       dsy *= 2.f;
       d_off[2 * gs] = dsx;
       d_off[2 * gs + 1] = dsy;
-      gqx += dsx;
-      gqy += dsy;
+#pragma unroll
+      for (int i = 0; i < QPW; ++i)
+        if (i == qi) { gqx[i] += dsx; gqy[i] += dsy; }
     }
     __syncwarp();
-    for (int t = lane; t < S * 4; t += 32) {
+    for (int t = lane; t < nq * S * 4; t += 32) {
       if (s_first[t] != t) continue;
       const int id = s_idx[t];
+      float* dkvb = d_kvpos + ((gq0 + (QPW == 1 ? 0 : t / (S * 4))) / Nq) * Nkv * 2;
       red_add(dkvb + 2 * id, s_w[t]);
       red_add(dkvb + 2 * id + 1, s_cf[t]);
     }
-    gqx = warp_sum(gqx);
-    gqy = warp_sum(gqy);
-    if (lane == 0) {
-      red_add(d_qpos + 2 * gq, gqx);
-      red_add(d_qpos + 2 * gq + 1, gqy);
+#pragma unroll
+    for (int i = 0; i < QPW; ++i) {
+      const float sx = warp_sum(gqx[i]), sy = warp_sum(gqy[i]);
+      if (lane == 0 && i < nq) {
+        red_add(d_qpos + 2 * (gq0 + i), sx);
+        red_add(d_qpos + 2 * (gq0 + i) + 1, sy);
+      }
     }
     __syncwarp();
   }
@@ -487,6 +509,14 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     for (int i = 0; i < DK_WARPS; ++i) t += s_pow[i];
     atomicAdd(d_power, t);
   }
+}
+
+// Queries per warp in the backward: enough for whole passes of 32 chunks
+// when the shared-memory slots allow (6 heads of 64 channels: 2).
+static int deform_bwd_queries_per_warp(int S, int nc8) {
+  int q = 1;
+  while (q < 4 && (q * nc8) % 32 != 0 && 2 * q * S <= DK_SMAX) q *= 2;
+  return q;
 }
 
 static int check_deform(int64_t B, int64_t Nq, int64_t Nkv, int64_t H, int64_t C) {
@@ -547,13 +577,20 @@ extern "C" int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos,
                "deform_knn_bwd: values/dout/d_values must be 16-byte aligned");
   if (B == 0 || Nq == 0) return AFFB_OK;
   cudaStream_t st = as_stream(stream);
-  const int64_t need = (B * Nq + DK_WARPS - 1) / DK_WARPS;
+  const int qpw = deform_bwd_queries_per_warp((int)H * 4, (int)(H * C / 8));
+  const int64_t need = (B * Nq + DK_WARPS * qpw - 1) / (DK_WARPS * qpw);
   const unsigned nb = (unsigned)imin64(need, (int64_t)sm_count() * 8);
-  AFFB_DISPATCH(dtype, T,
-                deform_knn_bwd_kernel<T><<<nb, DK_WARPS * 32, (size_t)DK_WARPS * H * 4 * 21 * sizeof(int), st>>>(
-                    query_pos, kv_pos, offsets, attn_w, (const T*)values, power, knn_idx, knn_d2,
-                    (const T*)dout, B, Nq, Nkv, (int)H, (int)C, d_offsets, d_attn_w, d_qpos,
-                    d_kvpos, d_values_acc, d_power));
+  const size_t smem = (size_t)DK_WARPS * qpw * H * 4 * 21 * sizeof(int);
+#define AFFB_DKB_LAUNCH(Q)                                                                          \
+  deform_knn_bwd_kernel<T, Q><<<nb, DK_WARPS * 32, smem, st>>>(                                      \
+      query_pos, kv_pos, offsets, attn_w, (const T*)values, power, knn_idx, knn_d2, (const T*)dout, B, \
+      Nq, Nkv, (int)H, (int)C, d_offsets, d_attn_w, d_qpos, d_kvpos, d_values_acc, d_power)
+  AFFB_DISPATCH(dtype, T, {
+    if (qpw == 1) AFFB_DKB_LAUNCH(1);
+    else if (qpw == 2) AFFB_DKB_LAUNCH(2);
+    else AFFB_DKB_LAUNCH(4);
+  });
+#undef AFFB_DKB_LAUNCH
   AFFB_LAUNCH_CHECK("affb_deform_knn_bwd");
   return AFFB_OK;
 }

@@ -305,7 +305,7 @@ class ClusterMerging(nn.Module):
     def __init__(self, dim: int, out_dim: int, ds_rate: float, inner: int = 4):
         super().__init__()
         self.ds_rate = ds_rate
-        self.weight_net = nn.Sequential(nn.Linear(5, inner), nn.LayerNorm(inner), nn.GELU())
+        self.weight_net = nn.Sequential(nn.Linear(5, inner), FusedLayerNorm(inner), nn.GELU())
         self.norm = FusedLayerNorm(inner * dim)
         self.linear = Linear(inner * dim, out_dim)
         self.register_buffer("rel_table", relative_position_table(), persistent=False)
@@ -478,6 +478,25 @@ def sine_embedding(pos: torch.Tensor, dim: int, dtype=torch.float32) -> torch.Te
         return torch.cat([t[..., 0::2].sin(), t[..., 1::2].cos()], -1)
     return torch.cat([enc(x), enc(y)], -1).to(dtype)
 
+class _SplitColumns(torch.autograd.Function):
+    """x[..., :k] and x[..., k:] as contiguous fp32 tensors (the deformable
+    kernels' offset and weight inputs); the gradient is one concatenation in
+    the dtype of x, instead of two zero-filled slice gradients summed."""
+
+    @staticmethod
+    def forward(ctx, x, k):
+        ctx.dtype, ctx.k, ctx.rest = x.dtype, k, x.shape[-1] - k
+        return x[..., :k].float().contiguous(), x[..., k:].float().contiguous()
+
+    @staticmethod
+    def backward(ctx, ga, gb):
+        if ga is None:
+            ga = gb.new_zeros(gb.shape[:-1] + (ctx.k,))
+        if gb is None:
+            gb = ga.new_zeros(ga.shape[:-1] + (ctx.rest,))
+        return torch.cat([ga, gb], -1).to(ctx.dtype), None
+
+
 class DeformableAttention(nn.Module):
     """Single-level deformable attention with 4 sampling points per head and
     Shepard (inverse-distance softmax) interpolation over the 4 nearest
@@ -511,8 +530,9 @@ class DeformableAttention(nn.Module):
         # over the two weight matrices stacked (one input gradient, not two summed)
         ow = _linear(query, torch.cat([self.sampling_offsets.weight, self.attention_weights.weight]),
                      torch.cat([self.sampling_offsets.bias, self.attention_weights.bias]))
-        off = ow[..., :H * P * 2].view(B, n, H, P, 2)
-        aw = F.softmax(ow[..., H * P * 2:].view(B, n, H, P), dim=-1)
+        off, logits = _SplitColumns.apply(ow, H * P * 2)            # fp32, contiguous
+        off = off.view(B, n, H, P, 2)
+        aw = F.softmax(logits.view(B, n, H, P), dim=-1)
         if kv is None:  # self attention
             vals = self.value_proj(query).view(B, n, H, C // H)
             out = fused_knn_deformable_self_attention(query_pos, off, aw, vals, self.shepard_power)

@@ -257,6 +257,46 @@ __global__ void pos_bias_bwd_kernel(const T* __restrict__ dbias, const int64_t* 
   for (int h = 0; h < H; ++h) red_add(dtable + e * H + h, ldf(dbias + (b * H + h) * N * M + nm));
 }
 
+// The same scatter for the reference's relative-position table (T = 255 x 255,
+// index (dy + 127) * 255 + dx + 127): neighbour lists name small offsets, so
+// most entries fall in the (2R+1)^2 offsets around the centre and all of a
+// block's entries for one offset would otherwise hit the same table row in
+// L2.  Each block sums those in shared memory and adds each sum to the table
+// once; entries outside the window go straight to global memory.
+constexpr int PB_TW = 255, PB_R = 16, PB_WIN = 2 * PB_R + 1;
+
+template <typename T>
+__global__ void __launch_bounds__(256) pos_bias_bwd_win_kernel(const T* __restrict__ dbias,
+                                                               const int64_t* __restrict__ pe, int64_t T_,
+                                                               int H, int64_t B, int64_t N, int64_t M,
+                                                               float* __restrict__ dtable) {
+  extern __shared__ float pb_acc[];  // [PB_WIN * PB_WIN][H]
+  for (int i = threadIdx.x; i < PB_WIN * PB_WIN * H; i += blockDim.x) pb_acc[i] = 0.f;
+  __syncthreads();
+  const int64_t NM = N * M, tot = B * NM;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < tot; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = t / NM, nm = t - b * NM;
+    int64_t e = pe[t];
+    if (e < 0 || e >= T_) e = e < 0 ? 0 : T_ - 1;
+    const int dy = (int)(e / PB_TW) - PB_TW / 2, dx = (int)(e % PB_TW) - PB_TW / 2;
+    const T* src = dbias + b * H * NM + nm;
+    if (dx >= -PB_R && dx <= PB_R && dy >= -PB_R && dy <= PB_R) {
+      float* a = pb_acc + ((dy + PB_R) * PB_WIN + dx + PB_R) * H;
+      for (int h = 0; h < H; ++h) atomicAdd(a + h, ldf(src + h * NM));
+    } else {
+      for (int h = 0; h < H; ++h) red_add(dtable + e * H + h, ldf(src + h * NM));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < PB_WIN * PB_WIN * H; i += blockDim.x) {
+    const float v = pb_acc[i];
+    if (v == 0.f) continue;
+    const int slot = i / H, h = i - slot * H;
+    const int dy = slot / PB_WIN - PB_R, dx = slot % PB_WIN - PB_R;
+    red_add(dtable + ((int64_t)(dy + PB_TW / 2) * PB_TW + dx + PB_TW / 2) * H + h, v);
+  }
+}
+
 static unsigned rows_blocks(int64_t rows) { return (unsigned)((rows + MW - 1) / MW); }
 
 }  // namespace affb
@@ -366,9 +406,17 @@ extern "C" int affb_pos_bias_bwd(const void* dbias, const int64_t* pe_idx, int d
   AFFB_REQUIRE(T >= 1 && H >= 1 && B >= 0 && N >= 0 && M >= 0, "pos_bias: invalid sizes");
   const int64_t tot = B * N * M;
   if (tot == 0) return AFFB_OK;
-  AFFB_DISPATCH(dtype, Tp,
-                pos_bias_bwd_kernel<Tp><<<(unsigned)((tot + 255) / 256), 256, 0, as_stream(stream)>>>(
-                    (const Tp*)dbias, pe_idx, T, (int)H, B, N, M, dtable_acc));
+  if (T == (int64_t)PB_TW * PB_TW && H <= 8) {
+    const unsigned blocks = (unsigned)imin64((tot + 255) / 256, (int64_t)sm_count() * 8);
+    const size_t smem = (size_t)PB_WIN * PB_WIN * H * sizeof(float);
+    AFFB_DISPATCH(dtype, Tp,
+                  pos_bias_bwd_win_kernel<Tp><<<blocks, 256, smem, as_stream(stream)>>>(
+                      (const Tp*)dbias, pe_idx, T, (int)H, B, N, M, dtable_acc));
+  } else {
+    AFFB_DISPATCH(dtype, Tp,
+                  pos_bias_bwd_kernel<Tp><<<(unsigned)((tot + 255) / 256), 256, 0, as_stream(stream)>>>(
+                      (const Tp*)dbias, pe_idx, T, (int)H, B, N, M, dtable_acc));
+  }
   AFFB_LAUNCH_CHECK("affb_pos_bias_bwd");
   return AFFB_OK;
 }

@@ -326,6 +326,10 @@ class ClusterMerging(nn.Module):
         # gather through the bias kernel ([B,inner,keep,M]); its backward is one
         # block-reduced scatter-add into the table instead of a sorted index_put
         weights = pos_bias_gather(table, pe).permute(0, 2, 3, 1) * lp     # [B,keep,M,inner]
+        if feat.is_cuda and torch.is_autocast_enabled("cuda"):
+            # under autocast the merge reads 16-bit features (the tensor-core
+            # kernel) whatever the dtype of the residual stream
+            feat = feat.to(torch.get_autocast_dtype("cuda"))
         merged = weighted_features(weights.to(feat.dtype), feat, member)  # [B,keep,inner,C]
         return pos_down, self.linear(self.norm(merged.reshape(B, keep, -1), out32=False, out16=True))
 

@@ -379,6 +379,25 @@ def test_pos_bias_gather(cuda):
     assert rel_err(t.grad.cpu(), oracle.pos_bias_bwd(g, pe, T)) < TOL_BWD
 
 
+@pytest.mark.parametrize("H", [4, 8, 12])
+def test_pos_bias_gather_small_offsets(cuda, H):
+    """Table gradient when the indices are the small relative offsets of
+    neighbour lists (the shared-memory window around the table centre, and
+    offsets just outside it), for head counts inside (4, 8) and beyond (12) the
+    window kernel's limit."""
+    from affmae_b200.kernels.pos_bias import pos_bias_gather
+    gen = torch.Generator().manual_seed(12 + H)
+    T, B, N, M = 255 * 255, 3, 257, 48
+    d = torch.randint(-20, 21, (B, N, M, 2), generator=gen)
+    pe = (d[..., 1] + 127) * 255 + d[..., 0] + 127
+    table = torch.randn((T, H), generator=gen)
+    t = table.to(cuda).requires_grad_()
+    out = pos_bias_gather(t, pe.to(cuda))
+    g = torch.randn((B, H, N, M), generator=gen)
+    out.backward(g.to(cuda))
+    assert rel_err(t.grad.cpu(), oracle.pos_bias_bwd(g, pe, T)) < TOL_BWD
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("mask_heads", [0, 1, 4])
 def test_local_attn_clustered_tensor_core_path(cuda, dtype, mask_heads):

@@ -410,6 +410,7 @@ __device__ void blk_fwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpFw
 
 template <typename T, int MM>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_FWD_MINB) nbhd_blk_fwd_kernel(NbhdArgs a) {
+  dependent_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlkFwdSmem<T, MM>& s = *reinterpret_cast<BlkFwdSmem<T, MM>*>(smem_raw);
   const int N = a.N;
@@ -557,6 +558,7 @@ __device__ void blk_bwd_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpBw
 // builder); otherwise the key-side and dQ kernels do the backward.
 template <typename T, int MM>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_BWD_MINB) nbhd_blk_bwd_kernel(NbhdArgs a) {
+  dependent_wait();
   if (!*a.general) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlkBwdSmem<T, MM>& s = *reinterpret_cast<BlkBwdSmem<T, MM>*>(smem_raw);
@@ -647,6 +649,7 @@ __device__ void blk_dq_head(const NbhdArgs& a, const BlkSetup<MM>& s, BlkWarpDq<
 
 template <typename T, int MM>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_DQ_MINB) nbhd_blk_dq_kernel(NbhdArgs a) {
+  dependent_wait();
   if (*a.general) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlkDqSmem<T, MM>& s = *reinterpret_cast<BlkDqSmem<T, MM>*>(smem_raw);
@@ -673,7 +676,10 @@ static int launch_blk(K kernel, size_t smem, const NbhdArgs& a, int B, cudaStrea
   }
   int64_t tiles = (int64_t)((a.N + TQ - 1) / TQ) * B;
   if (max_blocks > 0 && tiles > max_blocks) tiles = max_blocks;
-  kernel<<<(unsigned)tiles, TC_THREADS, smem, st>>>(a);
+  if (launch_dependent(kernel, dim3((unsigned)tiles), dim3(TC_THREADS), smem, st, a) != cudaSuccess) {
+    set_error("nbhd_attn: kernel failed to launch");
+    return AFFB_ERR_CUDA;
+  }
   return AFFB_OK;
 }
 

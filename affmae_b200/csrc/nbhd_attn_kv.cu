@@ -61,18 +61,17 @@ __device__ __forceinline__ void inv_count_block(const int32_t* __restrict__ midx
   const int64_t qn = valid ? t - (int64_t)b * N : 0;  // query index within its image
   const int J = M >> 3;
   const int4* row = reinterpret_cast<const int4*>(midx + (valid ? t : 0) * M);
-  int4 x[8], y[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    if (j < J) { x[j] = __ldg(row + 2 * j); y[j] = __ldg(row + 2 * j + 1); }
+  // one run at a time (two 16-byte loads): the launch shares its register
+  // budget with the prologue
   int cs[8];
   bool ok = true;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     cs[j] = 0;
     if (j < J) {
-      const int c0 = x[j].x;
-      const int v[8] = {x[j].x, x[j].y, x[j].z, x[j].w, y[j].x, y[j].y, y[j].z, y[j].w};
+      const int4 x = __ldg(row + 2 * j), y = __ldg(row + 2 * j + 1);
+      const int c0 = x.x;
+      const int v[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
       ok &= (c0 >= 0) & ((c0 & 7) == 0) & (c0 < N);
 #pragma unroll
       for (int r = 1; r < 8; ++r) {
@@ -119,6 +118,7 @@ __global__ void __launch_bounds__(1024) nbhd_inv_scan_kernel(const int* __restri
                                                              int* __restrict__ offs) {
   __shared__ int wsum[32];
   __shared__ int carry_s;
+  dependent_wait();
   if (*flag) return;
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int* cnt = counts + (int64_t)b * Cc;
@@ -158,6 +158,7 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
                                      const int* __restrict__ offs, const int* __restrict__ ecl,
                                      const int* __restrict__ erk, int* __restrict__ entries,
                                      float* __restrict__ acc_k, float* __restrict__ acc_v) {
+  dependent_wait();
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= (int64_t)B * N) return;
   const int b = (int)(t / N), q = (int)(t % N);
@@ -190,6 +191,10 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
 // registers over the block's rows and reduced once.
 constexpr int PRO_ROWS = 256;
 constexpr int PRO_PASSES = PRO_ROWS / 64;
+#ifndef AFFB_PRE_GROUP
+#define AFFB_PRE_GROUP 1  // passes whose loads are in flight together
+#endif
+constexpr int PRO_GROUP = AFFB_PRE_GROUP;
 
 template <typename T>
 __device__ __forceinline__ void cvt8(const uint4& u, float* o) {
@@ -214,6 +219,7 @@ __device__ __forceinline__ void cvt8(const uint4& u, float* o) {
 template <typename T>
 __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs& k, int64_t bid) {
   __shared__ float s_dbk[TD], s_dbv[TD];
+  __shared__ alignas(16) float s_bk[TD], s_bv[TD];
   const int N = a.N;
   const int nblk = (N + PRO_ROWS - 1) / PRO_ROWS;
   const int64_t bh = bid / nblk;
@@ -221,57 +227,71 @@ __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs
   const int t = threadIdx.x, lane = t & 31, sub = lane & 3;
   const int nbase = (int)(bid % nblk) * PRO_ROWS;
   const bool blank = a.blank_k != nullptr;
-  float bkv[8], bvv[8], gk[8], gv[8];
+  float gk[8], gv[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) { gk[e] = 0.f; gv[e] = 0.f; }
-  if (blank) {
-    ld8((const T*)a.blank_k + (int64_t)h * TD + sub * 8, bkv);
-    ld8((const T*)a.blank_v + (int64_t)h * TD + sub * 8, bvv);
-    if (t < TD) { s_dbk[t] = 0.f; s_dbv[t] = 0.f; }
+  // the blank token's k / v rows are read from shared memory where they are
+  // used, which keeps the register count within four blocks per SM
+  if (blank && t < TD) {
+    s_bk[t] = ldf((const T*)a.blank_k + (int64_t)h * TD + t);
+    s_bv[t] = ldf((const T*)a.blank_v + (int64_t)h * TD + t);
+    s_dbk[t] = 0.f;
+    s_dbv[t] = 0.f;
   }
-  uint4 ro[PRO_PASSES], rd[PRO_PASSES], rq[PRO_PASSES];
-  float ls[PRO_PASSES];
+  __syncthreads();
   const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  // rows in groups of PRO_GROUP passes: every load of a group is issued
+  // before the first is used
+#pragma unroll 1
+  for (int g0 = 0; g0 < PRO_PASSES; g0 += PRO_GROUP) {
+    uint4 ro[PRO_GROUP], rd[PRO_GROUP], rq[PRO_GROUP];
+    float ls[PRO_GROUP];
 #pragma unroll
-  for (int it = 0; it < PRO_PASSES; ++it) {
-    const int n = nbase + it * 64 + (t >> 2);
-    const int64_t row = bh * N + (n < N ? n : 0);
-    const bool valid = n < N;
-    ro[it] = valid ? __ldg(reinterpret_cast<const uint4*>((const T*)a.o + row * TD + sub * 8)) : z4;
-    rd[it] = valid ? __ldg(reinterpret_cast<const uint4*>((const T*)a.dout + row * TD + sub * 8)) : z4;
-    rq[it] = valid && blank ? __ldg(reinterpret_cast<const uint4*>((const T*)a.q + row * TD + sub * 8)) : z4;
-    ls[it] = valid && blank ? __ldg(a.lse + row) : 0.f;
-  }
+    for (int it = 0; it < PRO_GROUP; ++it) {
+      const int n = nbase + (g0 + it) * 64 + (t >> 2);
+      const int64_t row = bh * N + (n < N ? n : 0);
+      const bool valid = n < N;
+      ro[it] = valid ? __ldg(reinterpret_cast<const uint4*>((const T*)a.o + row * TD + sub * 8)) : z4;
+      rd[it] = valid ? __ldg(reinterpret_cast<const uint4*>((const T*)a.dout + row * TD + sub * 8)) : z4;
+      rq[it] = valid && blank ? __ldg(reinterpret_cast<const uint4*>((const T*)a.q + row * TD + sub * 8)) : z4;
+      ls[it] = valid && blank ? __ldg(a.lse + row) : 0.f;
+    }
 #pragma unroll
-  for (int it = 0; it < PRO_PASSES; ++it) {
-    const int n = nbase + it * 64 + (t >> 2);
-    const bool valid = n < N;
-    const int64_t row = bh * N + n;
-    float ov[8], dv[8], di = 0.f;
-    cvt8<T>(ro[it], ov);
-    cvt8<T>(rd[it], dv);
+    for (int it = 0; it < PRO_GROUP; ++it) {
+      const int n = nbase + (g0 + it) * 64 + (t >> 2);
+      const bool valid = n < N;
+      const int64_t row = bh * N + n;
+      float ov[8], dv[8], di = 0.f;
+      cvt8<T>(ro[it], ov);
+      cvt8<T>(rd[it], dv);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
-    di += __shfl_xor_sync(0xffffffffu, di, 1);
-    di += __shfl_xor_sync(0xffffffffu, di, 2);
-    if (valid && sub == 0) k.di[row] = di;
-    if (blank) {
-      float qv[8];
-      cvt8<T>(rq[it], qv);
-      float sb = 0.f, dpb = 0.f;
+      for (int e = 0; e < 8; ++e) di = fmaf(ov[e], dv[e], di);
+      di += __shfl_xor_sync(0xffffffffu, di, 1);
+      di += __shfl_xor_sync(0xffffffffu, di, 2);
+      if (valid && sub == 0) k.di[row] = di;
+      if (blank) {
+        float qv[8];
+        cvt8<T>(rq[it], qv);
+        const float4* bk4 = reinterpret_cast<const float4*>(s_bk + sub * 8);
+        const float4* bv4 = reinterpret_cast<const float4*>(s_bv + sub * 8);
+        const float4 k0 = bk4[0], k1 = bk4[1], v0 = bv4[0], v1 = bv4[1];
+        const float bkv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+        const float bvv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float sb = 0.f, dpb = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
+        for (int e = 0; e < 8; ++e) { sb = fmaf(qv[e], bkv[e], sb); dpb = fmaf(dv[e], bvv[e], dpb); }
 #pragma unroll
-      for (int o = 1; o < 4; o <<= 1) {
-        sb += __shfl_xor_sync(0xffffffffu, sb, o);
-        dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
-      }
-      if (valid) {
-        const float pb = expf(sb * a.scale - ls[it]);
-        const float dsb = pb * (dpb - di);
-        if (sub == 0) k.dsb[row] = dsb;
+        for (int o = 1; o < 4; o <<= 1) {
+          sb += __shfl_xor_sync(0xffffffffu, sb, o);
+          dpb += __shfl_xor_sync(0xffffffffu, dpb, o);
+        }
+        if (valid) {
+          const float pb = expf(sb * a.scale - ls[it]);
+          const float dsb = pb * (dpb - di);
+          if (sub == 0) k.dsb[row] = dsb;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) { gk[e] = fmaf(dsb, qv[e], gk[e]); gv[e] = fmaf(pb, dv[e], gv[e]); }
+          for (int e = 0; e < 8; ++e) { gk[e] = fmaf(dsb, qv[e], gk[e]); gv[e] = fmaf(pb, dv[e], gv[e]); }
+        }
       }
     }
   }
@@ -284,7 +304,6 @@ __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs
       gv[e] += __shfl_xor_sync(0xffffffffu, gv[e], o);
     }
   }
-  __syncthreads();
   if (lane < 4) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -304,7 +323,7 @@ __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs
 // The prologue does not wait for the list check: D, the blank dS and the
 // blank-token gradients are the same whichever kernels do the rest.
 template <typename T>
-__global__ void __launch_bounds__(256) nbhd_bwd_pre_kernel(NbhdArgs a, KvArgs k, NbhdBwdLayout ly,
+__global__ void __launch_bounds__(256, AFFB_PRE_MINB) nbhd_bwd_pre_kernel(NbhdArgs a, KvArgs k, NbhdBwdLayout ly,
                                                           int count_blocks, int B, int Cc) {
   if (blockIdx.x < count_blocks) {
     inv_count_block(a.midx, a.mask, a.mask_heads, B, a.N, a.M, Cc, ly.flag, ly.counts, ly.ecl, ly.erk,
@@ -488,6 +507,7 @@ __device__ __forceinline__ void kv_load_segment(KvSmem<T>& s, const int* src, in
 
 template <typename T>
 __global__ void __launch_bounds__(TC_THREADS, AFFB_KV_MINB) nbhd_kv_kernel(NbhdArgs a, KvArgs k) {
+  dependent_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   KvSmem<T>& s = *reinterpret_cast<KvSmem<T>*>(smem_raw);
   const int N = a.N, M = a.M, Cc = k.Cc;
@@ -576,7 +596,10 @@ int nbhd_kv_bwd(const NbhdArgs& a, const KvArgs& k, int dtype, int B, cudaStream
       set_error("nbhd_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
       return AFFB_ERR_CUDA;
     }
-    kernel<<<(unsigned)blocks, TC_THREADS, smem, st>>>(a, k);
+    if (launch_dependent(kernel, dim3((unsigned)blocks), dim3(TC_THREADS), smem, st, a, k) != cudaSuccess) {
+      set_error("nbhd_attn_bwd: key-side kernel failed to launch");
+      return AFFB_ERR_CUDA;
+    }
     return AFFB_OK;
   };
   if (dtype == AFFB_BF16) return go(nbhd_kv_kernel<__nv_bfloat16>, sizeof(KvSmem<__nv_bfloat16>));
@@ -597,9 +620,13 @@ int nbhd_bwd_prepare(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly
   const unsigned g = (unsigned)(cnt + pro);
   if (dtype == AFFB_BF16) nbhd_bwd_pre_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(a, k, ly, (int)cnt, B, Cc);
   else nbhd_bwd_pre_kernel<__half><<<g, 256, 0, st>>>(a, k, ly, (int)cnt, B, Cc);
-  nbhd_inv_scan_kernel<<<B, 1024, 0, st>>>(ly.counts, N, M >> 3, Cc, ly.flag, ly.offs);
-  nbhd_inv_fill_kernel<<<(unsigned)cnt, 256, 0, st>>>(B, N, M, Cc, a.H, ly.flag, ly.offs, ly.ecl, ly.erk,
-                                                     ly.entries, ly.acc_k, ly.acc_v);
+  if (launch_dependent(nbhd_inv_scan_kernel, dim3(B), dim3(1024), 0, st, ly.counts, N, M >> 3, Cc, ly.flag,
+                       ly.offs) != cudaSuccess ||
+      launch_dependent(nbhd_inv_fill_kernel, dim3((unsigned)cnt), dim3(256), 0, st, B, N, M, Cc, a.H, ly.flag,
+                       ly.offs, ly.ecl, ly.erk, ly.entries, ly.acc_k, ly.acc_v) != cudaSuccess) {
+    set_error("nbhd_attn_bwd: list kernels failed to launch");
+    return AFFB_ERR_CUDA;
+  }
   return AFFB_OK;
 }
 

@@ -31,6 +31,9 @@ constexpr int NW = TC_THREADS / 32;
 #ifndef AFFB_KV_MINB
 #define AFFB_KV_MINB 6  // 80 registers: 6 blocks of the key-side kernel per SM
 #endif
+#ifndef AFFB_PRE_MINB
+#define AFFB_PRE_MINB 4  // 64 registers: 4 blocks of 256 threads of the backward prologue per SM
+#endif
 
 template <typename T> struct MmaType;
 template <> struct MmaType<__nv_bfloat16> {

@@ -45,7 +45,10 @@ constexpr int DK_WARPS = 8;
 #define AFFB_DKB_MINB 4
 #endif
 constexpr int DKF_WARPS = AFFB_DKF_WARPS;
-constexpr int DK_SMAX = 64;  // samples per query (H * 4) handled per warp
+constexpr int DK_SMAX = 64;
+// backward shared memory per warp, in ints per sample slot: s_idx, s_first,
+// s_w, s_cf, s_dot, s_ulist (4 each), s_aw (1), s_ucnt (1, a quarter used)
+constexpr int DKB_SMEM_INTS = 26;  // samples per query (H * 4) handled per warp
 constexpr int DK_FWD_SLOTS = 128;  // forward: samples of the queries a warp handles together
 
 // Queries per warp in the forward: with H * 4 samples per query not a
@@ -337,7 +340,8 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
   // launch so the rest of the SM's shared/L1 storage caches values and
   // positions): s_idx, s_first (first entry of the head with the same kv row),
   // s_w, s_cf (merged aw * w of a first entry), s_dot (v[row] . dout[head] of
-  // a first entry): slots * 4 each; s_aw: slots
+  // a first entry), s_ulist (the first entries of each head, compacted):
+  // slots * 4 each; s_aw: slots; s_ucnt (first entries per head): slots / 4
   __shared__ float s_pow[DK_WARPS];
   extern __shared__ int dkb_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -345,12 +349,14 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
   const int S = H * 4;
   constexpr int qpw = QPW;
   const int slots = qpw * S;
-  int* s_idx = dkb_smem + warp * slots * 21;
+  int* s_idx = dkb_smem + warp * slots * DKB_SMEM_INTS;
   int* s_first = s_idx + slots * 4;
   float* s_w = reinterpret_cast<float*>(s_first + slots * 4);
   float* s_cf = s_w + slots * 4;
   float* s_dot = s_cf + slots * 4;
   float* s_aw = s_dot + slots * 4;
+  int* s_ulist = reinterpret_cast<int*>(s_aw + slots);
+  int* s_ucnt = s_ulist + slots * 4;
   const int row = H * C;
   const int nc8 = row / 8;
   const int G = C / 8;  // lanes (8-channel chunks) per head
@@ -379,13 +385,23 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     __syncwarp();
     // merge entries of a head that name the same kv row (entry e = slot * 4 + j;
     // the 16 entries of one head of one query are e >> 4)
-    for (int t = lane; t < nq * S * 4; t += 32) {
-      const int h0 = (t >> 4) << 4, id = s_idx[t];
+    // The first entries of each head are also listed compactly (s_ulist, count
+    // in s_ucnt): 32 lanes cover two heads' 16 entries.
+    for (int t0 = 0; t0 < nq * S * 4; t0 += 32) {
+      const int t = t0 + lane;
+      const bool in = t < nq * S * 4;
       int f = t;
-      for (int u = h0; u < t; ++u)
-        if (s_idx[u] == id) { f = u; break; }
-      s_first[t] = f;
-      atomicAdd(&s_cf[f], s_aw[t >> 2] * s_w[t]);
+      if (in) {
+        const int h0 = (t >> 4) << 4, id = s_idx[t];
+        for (int u = h0; u < t; ++u)
+          if (s_idx[u] == id) { f = u; break; }
+        s_first[t] = f;
+        atomicAdd(&s_cf[f], s_aw[t >> 2] * s_w[t]);
+      }
+      const unsigned firsts = __ballot_sync(0xffffffffu, in && f == t);
+      const unsigned half = (firsts >> (lane & 16)) & 0xffffu;
+      if (in && f == t) s_ulist[t & ~15 | __popc(half & ((1u << (lane & 15)) - 1u))] = t;
+      if (in && (lane & 15) == 0) s_ucnt[t >> 4] = __popc(half);
     }
     __syncwarp();
     // chunk u = qi * nc8 + c8; a head's G chunks stay in one aligned lane group
@@ -405,27 +421,47 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
 #pragma unroll
         for (int e = 0; e < 8; ++e) g[e] = 0.f;
       }
-      const int e0 = (qi * H + h) * 16;
-      for (int k = 0; k < 16; ++k) {
-        const int t = e0 + k;
-        const bool first = act && s_first[t] == t;
-        float dot = 0.f;
-        if (first) {
-          const int id = s_idx[t];
-          float v[8];
-          ld8(vb + (int64_t)id * row + c8 * 8, v);
+      // the head's distinct rows only, two per step: the two dot products are
+      // reduced over the head's G lanes together (the first exchange swaps
+      // halves, so one shuffle serves both)
+      const int hs = (qi * H + h) * 16;
+      const int cnt = act ? s_ucnt[hs >> 4] : 0;
+      const int kmax = __reduce_max_sync(0xffffffffu, cnt);
+      for (int k = 0; k < kmax; k += 2) {
+        float dd[2];
+        int tt[2];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) dot = fmaf(v[e], g[e], dot);
-          const float cf = s_cf[t];
-          float* dst = dvb + (int64_t)id * row + c8 * 8;
-          red_add_v4(dst, cf * g[0], cf * g[1], cf * g[2], cf * g[3]);
-          red_add_v4(dst + 4, cf * g[4], cf * g[5], cf * g[6], cf * g[7]);
+        for (int j = 0; j < 2; ++j) {
+          const bool on = k + j < cnt;
+          tt[j] = on ? s_ulist[hs + k + j] : -1;
+          dd[j] = 0.f;
+          if (on) {
+            const int id = s_idx[tt[j]];
+            float v[8];
+            ld8(vb + (int64_t)id * row + c8 * 8, v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dd[j] = fmaf(v[e], g[e], dd[j]);
+            const float cf = s_cf[tt[j]];
+            float* dst = dvb + (int64_t)id * row + c8 * 8;
+            red_add_v4(dst, cf * g[0], cf * g[1], cf * g[2], cf * g[3]);
+            red_add_v4(dst + 4, cf * g[4], cf * g[5], cf * g[6], cf * g[7]);
+          }
         }
-        if (shfl) {
-          for (int o = G >> 1; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (first && (lane % G) == 0) s_dot[t] = dot;
-        } else if (first) {
-          atomicAdd(&s_dot[t], dot);
+        if (shfl && G >= 2) {
+          const int o = G >> 1;
+          const bool hi = (lane & o) != 0;
+          float mine = hi ? dd[1] : dd[0];
+          mine += __shfl_xor_sync(0xffffffffu, hi ? dd[0] : dd[1], o);
+          for (int oo = o >> 1; oo > 0; oo >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, oo);
+          const int r = lane & (G - 1);
+          if (r == 0 && tt[0] >= 0) s_dot[tt[0]] = mine;
+          if (r == o && tt[1] >= 0) s_dot[tt[1]] = mine;
+        } else if (shfl) {  // G == 1: a lane holds the whole row of the head
+          if (tt[0] >= 0) s_dot[tt[0]] = dd[0];
+          if (tt[1] >= 0) s_dot[tt[1]] = dd[1];
+        } else {
+          if (tt[0] >= 0) atomicAdd(&s_dot[tt[0]], dd[0]);
+          if (tt[1] >= 0) atomicAdd(&s_dot[tt[1]], dd[1]);
         }
       }
     }
@@ -580,7 +616,7 @@ extern "C" int affb_deform_knn_bwd(const float* query_pos, const float* kv_pos,
   const int qpw = deform_bwd_queries_per_warp((int)H * 4, (int)(H * C / 8));
   const int64_t need = (B * Nq + DK_WARPS * qpw - 1) / (DK_WARPS * qpw);
   const unsigned nb = (unsigned)imin64(need, (int64_t)sm_count() * 8);
-  const size_t smem = (size_t)DK_WARPS * qpw * H * 4 * 21 * sizeof(int);
+  const size_t smem = (size_t)DK_WARPS * qpw * H * 4 * DKB_SMEM_INTS * sizeof(int);
 #define AFFB_DKB_LAUNCH(Q)                                                                          \
   deform_knn_bwd_kernel<T, Q><<<nb, DK_WARPS * 32, smem, st>>>(                                      \
       query_pos, kv_pos, offsets, attn_w, (const T*)values, power, knn_idx, knn_d2, (const T*)dout, B, \

@@ -15,6 +15,9 @@ GB/s; the same command under ``ncu -k <kernel>`` gives the kernel profiles.
   wfeat-fwd  the same, forward only
   wgather    config 1: idx [2,1024,48], softmax weights, feat [2,4096,128] fp32, fwd+bwd
   layer-norm  config 5 stage 1: residual + dropout + LayerNorm, 524288 rows of 96, fwd+bwd
+  layer-norm-dec  the same at the decoder width (524288 rows of 384)
+  res-norm    config 5 stage 1 pre-norm residual (s = x + delta kept in fp32, y = LN(s) in bf16), fwd+bwd
+  res-norm-s3 the same at stage 3 (16 x 5243 rows of 384)
   rel-bias    config 5 stage 1: in-kernel relative-position bias [16,3,32768,48], fwd+bwd
   head-layout config 5 stage 1: kv head split + output merge, [16,32768,3x32], fwd+bwd
   deform-nbidx  deformable attention with given 4-NN indices (non-fused path), fwd+bwd
@@ -158,12 +161,13 @@ def op_wgather():
     return step, fwd + bwd, {"B": B, "M": Mq, "K": K, "N": N, "C": C, "dtype": "fp32", "pass": "fwd+bwd"}
 
 
-def op_layer_norm():
-    """Config 5 stage 1: LayerNorm(x + dropout(delta)) over 16 x 32768 tokens of C=96,
-    fp32 residual stream and bf16 delta, fp32 + bf16 outputs, fwd+bwd."""
+def op_layer_norm(C=96):
+    """Config 5 stage 1 (C=96) or decoder (C=384): LayerNorm(x + dropout(delta))
+    over 16 x 32768 tokens, fp32 residual stream and bf16 delta, fp32 + bf16
+    outputs, fwd+bwd."""
     from .kernels.layer_norm import fused_layer_norm
     g = torch.Generator().manual_seed(0)
-    R, C = 16 * 32768, 96
+    R = 16 * 32768
     x = torch.randn((R, C), generator=g).to("cuda").requires_grad_(True)
     d = torch.randn((R, C), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
     w = torch.ones(C, device="cuda", requires_grad=True)
@@ -178,6 +182,28 @@ def op_layer_norm():
     fwd = R * C * (4 + 2 + 4 + 4 + 2)
     bwd = R * C * (4 + 2 + 4 + 4 + 2)
     return step, fwd + bwd, {"rows": R, "C": C, "x": "fp32", "delta": "bf16", "p": 0.1, "pass": "fwd+bwd"}
+
+
+def op_residual_norm(R=16 * 32768, C=96):
+    """Pre-norm residual block of the encoder: (s, y) = (x + delta, LayerNorm(s))
+    with s fp32 kept, y bf16; the backward takes ds and dy.  Config 5 stage 1
+    (16 x 32768 tokens, C=96) or stage 3 (16 x 5243 tokens, C=384)."""
+    from .kernels.layer_norm import ResidualNormFunction
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((R, C), generator=g).to("cuda").requires_grad_(True)
+    d = torch.randn((R, C), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
+    w = torch.ones(C, device="cuda", requires_grad=True)
+    b = torch.zeros(C, device="cuda", requires_grad=True)
+    gs = torch.randn((R, C), generator=g).to("cuda")
+    gy = torch.randn((R, C), generator=g).to("cuda", torch.bfloat16)
+
+    def step():
+        s, y = ResidualNormFunction.apply(x, d, None, w, b, 1e-5)
+        torch.autograd.backward((s, y), (gs, gy))
+    # fwd: x, delta in; s, y16 out; bwd: ds, dy16, s in; dx, ddelta out
+    fwd = R * C * (4 + 2 + 4 + 2)
+    bwd = R * C * (4 + 2 + 4 + 4 + 2)
+    return step, fwd + bwd, {"rows": R, "C": C, "x": "fp32", "delta": "bf16", "pass": "fwd+bwd"}
 
 
 def op_rel_bias():
@@ -244,7 +270,9 @@ def op_deform_nbidx():
 
 
 OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_deform, "deform-mae": op_deform_mae,
-       "deform-mae-raster": lambda: op_deform_mae(raster=True), "wfeat": op_wfeat,
+       "deform-mae-raster": lambda: op_deform_mae(raster=True),
+       "layer-norm-dec": lambda: op_layer_norm(C=384), "res-norm": op_residual_norm,
+       "res-norm-s3": lambda: op_residual_norm(R=16 * 5243, C=384), "wfeat": op_wfeat,
        "wfeat-fwd": lambda: op_wfeat(fwd_only=True),
        "wgather": op_wgather, "layer-norm": op_layer_norm, "rel-bias": op_rel_bias,
        "head-layout": op_head_layout, "deform-nbidx": op_deform_nbidx, "tile-union": None}

@@ -467,8 +467,10 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
     }
     __syncwarp();
     // d_kv_pos is summed per distinct kv row of a head in shared memory (in
-    // s_w / s_cf, no longer read) and scattered once per row below
-    for (int t = lane; t < nq * S * 4; t += 32) { s_w[t] = 0.f; s_cf[t] = 0.f; }
+    // s_ulist / s_cf, no longer read) and scattered once per row below; s_w
+    // still holds the Shepard weights of the first pass
+    float* s_gx = reinterpret_cast<float*>(s_ulist);
+    for (int t = lane; t < nq * S * 4; t += 32) { s_gx[t] = 0.f; s_cf[t] = 0.f; }
     __syncwarp();
     float gqx[QPW], gqy[QPW];   // this lane's share of d_query_pos per query
 #pragma unroll
@@ -481,11 +483,24 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       const int64_t gs = gq0 * S + t;
       const float sx = __fadd_rn(qx, offsets[2 * gs]);
       const float sy = __fadd_rn(qy, offsets[2 * gs + 1]);
-      const int4 ii = make_int4(s_idx[t * 4], s_idx[t * 4 + 1], s_idx[t * 4 + 2], s_idx[t * 4 + 3]);
-      float d2[4];
-      load_d2(knn_d2, gs, ii, kvb, qx, qy, offsets, d2);
-      float w[4], dist[4];
-      shepard4(d2, P, w, dist);
+      // sample-to-neighbour vectors; the squared distances from them carry
+      // the forward's rounding (sqdist2), unless the saved ones are given
+      float exv[4], eyv[4], d2[4], w[4], dist[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int id = s_idx[t * 4 + j];
+        const float px = kvb[2 * id], py = kvb[2 * id + 1];
+        exv[j] = sx - px;
+        eyv[j] = sy - py;
+        d2[j] = sqdist2(sx, sy, px, py);
+        w[j] = s_w[t * 4 + j];
+      }
+      if (knn_d2) {
+        const float4 dd = reinterpret_cast<const float4*>(knn_d2)[gs];
+        d2[0] = dd.x; d2[1] = dd.y; d2[2] = dd.z; d2[3] = dd.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dist[j] = sqrtf(d2[j]) + 1e-6f;  // as in shepard4
       const float aw = s_aw[t];
       float dot[4], datt = 0.f;
 #pragma unroll
@@ -503,12 +518,11 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
         const float ds = w[j] * (dp[j] - wdp);
         dpow += ds * (-dist[j]);
         const float dd2 = (ds * (-P)) / (2.f * dist[j]);
-        const int id = s_idx[t * 4 + j];
-        const float ex = sx - kvb[2 * id], ey = sy - kvb[2 * id + 1];
+        const float ex = exv[j], ey = eyv[j];
         dsx = fmaf(ex, dd2, dsx);
         dsy = fmaf(ey, dd2, dsy);
         const int f = s_first[t * 4 + j];
-        atomicAdd(&s_w[f], -2.f * ex * dd2);
+        atomicAdd(&s_gx[f], -2.f * ex * dd2);
         atomicAdd(&s_cf[f], -2.f * ey * dd2);
       }
       dsx *= 2.f;
@@ -524,7 +538,7 @@ deform_knn_bwd_kernel(const float* __restrict__ qpos, const float* __restrict__ 
       if (s_first[t] != t) continue;
       const int id = s_idx[t];
       float* dkvb = d_kvpos + ((gq0 + (QPW == 1 ? 0 : t / (S * 4))) / Nq) * Nkv * 2;
-      red_add(dkvb + 2 * id, s_w[t]);
+      red_add(dkvb + 2 * id, s_gx[t]);
       red_add(dkvb + 2 * id + 1, s_cf[t]);
     }
 #pragma unroll

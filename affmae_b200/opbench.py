@@ -13,6 +13,8 @@ GB/s; the same command under ``ncu -k <kernel>`` gives the kernel profiles.
   deform-mae-raster  the same with the queries in raster order
   wfeat      config 5 stage-1 merging: weights [16,13107,48,4], feat [16,32768,96] bf16, fwd+bwd
   wfeat-fwd  the same, forward only
+  wfeat-lists / wfeat-lists-fwd  the same with the merging step's own index lists (the stage-1
+             neighbourhoods of the kept tokens: 6 runs of 8 consecutive rows) instead of random rows
   wgather    config 1: idx [2,1024,48], softmax weights, feat [2,4096,128] fp32, fwd+bwd
   layer-norm  config 5 stage 1: residual + dropout + LayerNorm, 524288 rows of 96, fwd+bwd
   layer-norm-dec  the same at the decoder width (524288 rows of 384)
@@ -121,13 +123,22 @@ def op_deform_mae(raster=False):
                              "queries": "masked patches of a 256x256 lattice, " + ("raster order" if raster else "random order")}
 
 
-def op_wfeat(fwd_only=False):
+def op_wfeat(fwd_only=False, lists=False):
     from .kernels.weighted_features import weighted_features
     g = torch.Generator().manual_seed(0)
     B, No, M, IC, N, C = 16, 13107, 48, 4, 32768, 96
     w = torch.randn((B, No, M, IC), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
     f = torch.randn((B, N, C), generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
-    idx = torch.randint(0, N, (B, No, M), generator=g).to("cuda")
+    if lists:
+        # the merging step's own index lists: the neighbourhoods of stage 1
+        # (256 x 256 patch grid at a 0.5 mask, clusters of 8 along the
+        # reference's anchor scan, 6 nearest clusters) of 13107 kept tokens
+        from .workloads import clustered_tokens, neighbourhoods
+        member, _ = neighbourhoods(clustered_tokens(B, 256, 0.5, 0, "cuda", "curve"), 8, M)
+        keep = torch.rand((B, N), generator=g).argsort(1)[:, :No].sort(1).values.to("cuda")
+        idx = member.gather(1, keep[..., None].expand(-1, -1, M)).long()
+    else:
+        idx = torch.randint(0, N, (B, No, M), generator=g).to("cuda")
     dout = torch.randn((B, No, IC, C), generator=g).to("cuda", torch.bfloat16)
 
     if fwd_only:
@@ -135,14 +146,15 @@ def op_wfeat(fwd_only=False):
             with torch.no_grad():
                 weighted_features(w, f, idx)
         return step, _nbytes(w, f, idx, dout), {"B": B, "No": No, "M": M, "IC": IC, "N": N, "C": C,
-                                                "dtype": "bf16", "pass": "fwd"}
+                                                "dtype": "bf16", "pass": "fwd",
+                                                "indices": "stage-1 lists" if lists else "random"}
 
     def step():
         weighted_features(w, f, idx).backward(dout)
     fwd = _nbytes(w, f, idx, dout)
     bwd = _nbytes(dout, w, f, idx) + _nbytes(w, f)
     return step, fwd + bwd, {"B": B, "No": No, "M": M, "IC": IC, "N": N, "C": C, "dtype": "bf16",
-                             "pass": "fwd+bwd"}
+                             "pass": "fwd+bwd", "indices": "stage-1 lists" if lists else "random"}
 
 
 def op_wgather():
@@ -274,6 +286,7 @@ OPS = {"knn": op_knn, "knn-brute": lambda: op_knn(brute=True), "deform": op_defo
        "layer-norm-dec": lambda: op_layer_norm(C=384), "res-norm": op_residual_norm,
        "res-norm-s3": lambda: op_residual_norm(R=16 * 5243, C=384), "wfeat": op_wfeat,
        "wfeat-fwd": lambda: op_wfeat(fwd_only=True),
+       "wfeat-lists": lambda: op_wfeat(lists=True), "wfeat-lists-fwd": lambda: op_wfeat(fwd_only=True, lists=True),
        "wgather": op_wgather, "layer-norm": op_layer_norm, "rel-bias": op_rel_bias,
        "head-layout": op_head_layout, "deform-nbidx": op_deform_nbidx, "tile-union": None}
 

@@ -26,10 +26,10 @@ constexpr int NW = TC_THREADS / 32;
 #define AFFB_BWD_MINB 1
 #endif
 #ifndef AFFB_DQ_MINB
-#define AFFB_DQ_MINB 10  // 48 registers: 10 dQ tiles per SM
+#define AFFB_DQ_MINB 12  // 40 registers: 12 dQ tiles per SM (a few bytes spilled; 3.4 us faster at config 3 than 10 tiles at 48)
 #endif
 #ifndef AFFB_KV_MINB
-#define AFFB_KV_MINB 6  // 80 registers: 6 blocks of the key-side kernel per SM
+#define AFFB_KV_MINB 7  // 72 registers: 7 blocks of the key-side kernel per SM (8 blocks at 64 spill and run slower)
 #endif
 #ifndef AFFB_PRE_MINB
 #define AFFB_PRE_MINB 4  // 64 registers: 4 blocks of 256 threads of the backward prologue per SM

@@ -179,6 +179,14 @@ __global__ void nbhd_inv_fill_kernel(int B, int N, int M, int Cc, int H, const i
   }
 }
 
+// Clears n 16-byte words (the list flag and counters of one call).
+__global__ void nbhd_zero_kernel(uint4* __restrict__ p, int64_t n) {
+  dependent_wait();
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = z;
+}
+
 // ------------------------------------------------------ query prologue --
 
 // Per (b, h, n): D = rowsum(O * dO) and, with a blank token, its probability
@@ -325,6 +333,7 @@ __device__ __forceinline__ void q_prologue_block(const NbhdArgs& a, const KvArgs
 template <typename T>
 __global__ void __launch_bounds__(256, AFFB_PRE_MINB) nbhd_bwd_pre_kernel(NbhdArgs a, KvArgs k, NbhdBwdLayout ly,
                                                           int count_blocks, int B, int Cc) {
+  dependent_wait();
   if (blockIdx.x < count_blocks) {
     inv_count_block(a.midx, a.mask, a.mask_heads, B, a.N, a.M, Cc, ly.flag, ly.counts, ly.ecl, ly.erk,
                     blockIdx.x);
@@ -610,16 +619,25 @@ int nbhd_bwd_prepare(const NbhdArgs& a, const KvArgs& k, const NbhdBwdLayout& ly
                      cudaStream_t st) {
   const int N = a.N, M = a.M, Cc = k.Cc;
   const int64_t rows = (int64_t)B * N;
-  if (cudaMemsetAsync(ly.flag, 0, ly.zero_bytes, st) != cudaSuccess) {
-    set_error("nbhd_attn_bwd: cudaMemsetAsync failed");
+  // the list flag and counters are cleared by a kernel (not a memset) so the
+  // whole chain, from the forward on, runs under programmatic dependent launch
+  const int64_t z16 = (int64_t)(ly.zero_bytes / 16);
+  if (launch_dependent(nbhd_zero_kernel, dim3((unsigned)imin64((z16 + 255) / 256, (int64_t)sm_count() * 4)),
+                       dim3(256), 0, st, reinterpret_cast<uint4*>(ly.flag), z16) != cudaSuccess) {
+    set_error("nbhd_attn_bwd: list counter clear failed to launch");
     return AFFB_ERR_CUDA;
   }
   const int64_t cnt = (rows + 255) / 256;
   const int64_t pro = (int64_t)B * a.H * ((N + PRO_ROWS - 1) / PRO_ROWS);
   AFFB_REQUIRE(cnt + pro < (1ll << 31), "nbhd_attn_bwd: too many rows");
   const unsigned g = (unsigned)(cnt + pro);
-  if (dtype == AFFB_BF16) nbhd_bwd_pre_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(a, k, ly, (int)cnt, B, Cc);
-  else nbhd_bwd_pre_kernel<__half><<<g, 256, 0, st>>>(a, k, ly, (int)cnt, B, Cc);
+  const cudaError_t le = dtype == AFFB_BF16
+      ? launch_dependent(nbhd_bwd_pre_kernel<__nv_bfloat16>, dim3(g), dim3(256), 0, st, a, k, ly, (int)cnt, B, Cc)
+      : launch_dependent(nbhd_bwd_pre_kernel<__half>, dim3(g), dim3(256), 0, st, a, k, ly, (int)cnt, B, Cc);
+  if (le != cudaSuccess) {
+    set_error("nbhd_attn_bwd: list count / prologue kernel failed to launch");
+    return AFFB_ERR_CUDA;
+  }
   if (launch_dependent(nbhd_inv_scan_kernel, dim3(B), dim3(1024), 0, st, ly.counts, N, M >> 3, Cc, ly.flag,
                        ly.offs) != cudaSuccess ||
       launch_dependent(nbhd_inv_fill_kernel, dim3((unsigned)cnt), dim3(256), 0, st, B, N, M, Cc, a.H, ly.flag,

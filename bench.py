@@ -46,10 +46,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "nbr-attn fwd+bwd HBM GB/s"
-# our kernels per timed step: the forward, and in the backward the list count +
-# prologue, the list scan and fill, the query-side kernel (returns at once for
-# cluster-run lists), the key-side kernel and the dQ kernel
-LAUNCHES_PER_STEP = 7
+# our kernels per timed step: the forward, and in the backward the list-counter
+# clear, the list count + prologue, the list scan and fill, the query-side kernel
+# (returns at once for cluster-run lists), the key-side kernel and the dQ kernel
+LAUNCHES_PER_STEP = 8
 CFG = dict(B=32, side=96, keep=0.5, H=4, d=32, nbhd=48)
 # DRAM bytes (read + write) of one backward call per image, from one ncu capture of
 # every backward kernel at B=16 (profiles/nbhd_attn_kernels_config3_b16.md: 286.2 MB);
